@@ -1,0 +1,256 @@
+// C-ABI entry points of the B200 GDN hot path (declared in include/gdn_b200.h):
+// host-side validation, TMA tensor-map construction and kernel launches.
+// One translation unit so that a single device status word serves every kernel.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "gdn_b200.h"
+#include "decode_kernel.cuh"
+#include "prefill_kernel.cuh"
+
+namespace gdn {
+
+__device__ unsigned int g_status;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(GDN_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+// Per-device one-time setup: address of the status word, dynamic smem opt-in.
+struct DeviceSetup {
+  bool done = false;
+  unsigned int* status = nullptr;
+};
+DeviceSetup g_setup[kMaxDevices];
+std::mutex g_setup_mu;
+
+int device_setup(unsigned int** status_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(GDN_B200_ERR_CUDA, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  DeviceSetup& s = g_setup[dev];
+  if (!s.done) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    e = cudaFuncSetAttribute(gdn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kPrefillSmem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill smem)");
+    s.status = static_cast<unsigned int*>(addr);
+    s.done = true;
+  }
+  *status_out = s.status;
+  return GDN_B200_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Tensor map over a packed [tokens, heads, 128] bf16 tensor; box = 64 tokens x
+// 1 head x 64 features (128 bytes, the 128B-swizzle span).
+int make_token_map(CUtensorMap* m, const void* base, int heads, long long tokens) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return fail(GDN_B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(tokens)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHeadDim) * 2,
+                           static_cast<cuuint64_t>(heads) * kHeadDim * 2};
+  cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kChunk)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GDN_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  return GDN_B200_OK;
+}
+
+int check_heads(int32_t h_qk, int32_t h_v, int32_t d) {
+  if (d != kHeadDim) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "head_dim must be 128");
+  if (h_qk <= 0 || h_v <= 0)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "head counts must be positive");
+  if (h_v % h_qk != 0)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_v_heads must be a multiple of num_qk_heads");
+  return GDN_B200_OK;
+}
+
+float resolve_scale(double scale) {
+  float s = static_cast<float>(scale);
+  if (s == 0.0f) s = 1.0f / std::sqrt(static_cast<float>(kHeadDim));
+  return s;
+}
+
+}  // namespace
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" int gdn_b200_decode(const void* q, const void* k, const void* v, const float* state,
+                               const float* A_log, const void* a, const float* dt_bias,
+                               const void* b, double scale, void* output, float* new_state,
+                               int64_t batch, int32_t num_qk_heads, int32_t num_v_heads,
+                               int32_t head_dim, void* stream) {
+  t_last_error.clear();
+  if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
+  if (batch < 0) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch must be >= 0");
+  if (batch * num_v_heads > 0x7fffffffLL)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch * num_v_heads exceeds the grid limit");
+  if (batch == 0) return GDN_B200_OK;
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !new_state)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(new_state, 16) ||
+      (state && !aligned(state, 16)))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "q/k need 8-byte and state/new_state 16-byte alignment");
+  unsigned int* status = nullptr;
+  if (int rc = device_setup(&status)) return rc;
+  DecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.state = state;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.scale = resolve_scale(scale);
+  p.out = static_cast<__nv_bfloat16*>(output);
+  p.new_state = new_state;
+  p.h_qk = num_qk_heads;
+  p.h_v = num_v_heads;
+  const dim3 grid(static_cast<unsigned>(batch * num_v_heads));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (state)
+    gdn_decode_kernel<true><<<grid, kDecodeThreads, 0, st>>>(p);
+  else
+    gdn_decode_kernel<false><<<grid, kDecodeThreads, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return GDN_B200_OK;
+}
+
+extern "C" int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* state,
+                                const float* A_log, const void* a, const float* dt_bias,
+                                const void* b, const void* cu_seqlens,
+                                int32_t cu_seqlens_is_int64, double scale, void* output,
+                                float* new_state, int64_t num_seqs, int64_t total_tokens,
+                                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                                void* stream) {
+  t_last_error.clear();
+  if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
+  if (num_seqs < 0 || total_tokens < 0)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0");
+  if (num_seqs > 65535)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs exceeds 65535");
+  if (total_tokens > 0x7fffffffLL - kChunk)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "total_tokens exceeds the int32 TMA coordinate range");
+  if (num_seqs == 0) return GDN_B200_OK;
+  if (!cu_seqlens || !A_log || !dt_bias || !new_state)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !output))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null token tensor with total_tokens > 0");
+  if ((total_tokens > 0 && (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) ||
+                            !aligned(output, 16))) ||
+      !aligned(new_state, 16) || (state && !aligned(state, 16)))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "q/k/v/output/state/new_state need 16-byte alignment");
+  if (!aligned(cu_seqlens, cu_seqlens_is_int64 ? 8 : 4))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "cu_seqlens is misaligned");
+  unsigned int* status = nullptr;
+  if (int rc = device_setup(&status)) return rc;
+
+  // With no tokens every sequence is empty; the maps still need a valid extent,
+  // so they describe a one-token view of new_state's (aligned) memory, which no
+  // CTA reads because every sequence returns before its first load.
+  const long long map_tokens = total_tokens > 0 ? total_tokens : 1;
+  const void* qb = total_tokens > 0 ? q : new_state;
+  const void* kb = total_tokens > 0 ? k : new_state;
+  const void* vb = total_tokens > 0 ? v : new_state;
+  CUtensorMap tq, tk, tv;
+  if (int rc = make_token_map(&tq, qb, total_tokens > 0 ? num_qk_heads : 1, map_tokens)) return rc;
+  if (int rc = make_token_map(&tk, kb, total_tokens > 0 ? num_qk_heads : 1, map_tokens)) return rc;
+  if (int rc = make_token_map(&tv, vb, total_tokens > 0 ? num_v_heads : 1, map_tokens)) return rc;
+
+  PrefillParams p;
+  p.state = state;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.cu_seqlens = cu_seqlens;
+  p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
+  p.total_tokens = total_tokens;
+  p.scale = resolve_scale(scale);
+  p.out = static_cast<__nv_bfloat16*>(output);
+  p.new_state = new_state;
+  p.h_qk = num_qk_heads;
+  p.h_v = num_v_heads;
+  p.status = status;
+  const dim3 grid(static_cast<unsigned>(num_v_heads), static_cast<unsigned>(num_seqs));
+  gdn_prefill_kernel<<<grid, kPrefillThreads, kPrefillSmem, static_cast<cudaStream_t>(stream)>>>(
+      tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return GDN_B200_OK;
+}
+
+extern "C" int gdn_b200_device_status(int32_t device, uint32_t* status, int32_t clear) {
+  t_last_error.clear();
+  if (!status) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "status is null");
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (device != prev && (e = cudaSetDevice(device)) != cudaSuccess)
+    return cuda_fail(e, "cudaSetDevice");
+  unsigned int v = 0;
+  e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+  if (e == cudaSuccess && clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+  }
+  if (device != prev) cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "device status");
+  *status = v;
+  return GDN_B200_OK;
+}
+
+extern "C" const char* gdn_b200_last_error(void) { return t_last_error.c_str(); }
+
+extern "C" int32_t gdn_b200_abi_version(void) { return 100; }

@@ -1,0 +1,163 @@
+"""Host-side mirror of the reference's ``kernel`` entry points.
+
+The reference exports one TVM-FFI function named ``kernel`` per path, in
+destination-passing style (all inputs, then the pre-allocated outputs):
+
+* decode  (ref solution/cuda/kernel.cu:101-113):
+  ``kernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)``
+* prefill (ref solution/cuda/kernel_prefill.cu:300-305):
+  ``kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)``
+
+``gdn_decode`` / ``gdn_prefill`` here take exactly those arguments (torch CUDA
+tensors), validate them like the TVM-FFI exports of this package do (raising
+``ValueError``), and call the C ABI of ``libgdn_b200.so`` on the current torch
+stream.  ``decode`` / ``prefill`` are allocating conveniences on top.
+``load_tvm_kernel`` returns the TVM-FFI ``kernel`` itself, which is what the
+reference's harness binds.
+
+Semantics as in the reference: ``scale == 0`` means 1/sqrt(128); ``state`` may
+be ``None`` (zero initial state); ``new_state`` may be ``state`` itself
+(in-place); in prefill an empty sequence copies its initial state.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+HEAD_DIM = 128
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _check(t: torch.Tensor, name: str, dtype, shape, device) -> None:
+    _require(isinstance(t, torch.Tensor), f"{name}: expected a torch.Tensor")
+    _require(t.dtype == dtype, f"{name}: expected {dtype}, got {t.dtype}")
+    _require(t.device == device, f"{name}: must be on {device}, got {t.device}")
+    _require(tuple(t.shape) == tuple(shape), f"{name}: expected shape {tuple(shape)}, got {tuple(t.shape)}")
+    _require(t.numel() == 0 or t.is_contiguous(), f"{name}: must be contiguous")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _cuda_device(q: torch.Tensor):
+    _require(isinstance(q, torch.Tensor) and q.is_cuda, "q must be a CUDA tensor")
+    return q.device
+
+
+def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state) -> None:
+    """One T=1 decode step; same arguments as the reference decode ``kernel``.
+
+    q, k: [B, 1, H_qk, 128] bf16; v: [B, 1, H_v, 128] bf16; state: [B, H_v, 128, 128]
+    fp32 or None; A_log, dt_bias: [H_v] fp32; a, b: [B, 1, H_v] bf16;
+    output: [B, 1, H_v, 128] bf16; new_state: [B, H_v, 128, 128] fp32 (may be state).
+    """
+    dev = _cuda_device(q)
+    _require(q.dim() == 4 and v.dim() == 4, "q and v must be [B, 1, H, D]")
+    B, T, h_qk, D = q.shape
+    h_v = v.shape[2]
+    _require(T == 1, "decode takes T == 1")
+    _check(q, "q", torch.bfloat16, (B, 1, h_qk, D), dev)
+    _check(k, "k", torch.bfloat16, (B, 1, h_qk, D), dev)
+    _check(v, "v", torch.bfloat16, (B, 1, h_v, D), dev)
+    _check(A_log, "A_log", torch.float32, (h_v,), dev)
+    _check(a, "a", torch.bfloat16, (B, 1, h_v), dev)
+    _check(dt_bias, "dt_bias", torch.float32, (h_v,), dev)
+    _check(b, "b", torch.bfloat16, (B, 1, h_v), dev)
+    _check(output, "output", torch.bfloat16, (B, 1, h_v, D), dev)
+    _check(new_state, "new_state", torch.float32, (B, h_v, D, D), dev)
+    if state is not None:
+        _check(state, "state", torch.float32, (B, h_v, D, D), dev)
+    lib = _lib.load()
+    _lib.check(lib.gdn_b200_decode(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
+        float(scale or 0.0), _ptr(output), _ptr(new_state), B, h_qk, h_v, D, _stream(dev)))
+
+
+def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                new_state) -> None:
+    """Chunked prefill; same arguments as the reference prefill ``kernel``.
+
+    q, k: [T, H_qk, 128] bf16 (packed tokens); v: [T, H_v, 128] bf16;
+    state: [N, H_v, 128, 128] fp32 or None; a, b: [T, H_v] bf16;
+    cu_seqlens: [N + 1] int32 or int64 on the same device;
+    output: [T, H_v, 128] bf16; new_state: [N, H_v, 128, 128] fp32 (may be state).
+    """
+    dev = _cuda_device(q)
+    _require(q.dim() == 3 and v.dim() == 3, "q and v must be packed [T, H, D]")
+    T, h_qk, D = q.shape
+    h_v = v.shape[1]
+    _require(isinstance(cu_seqlens, torch.Tensor) and cu_seqlens.dim() == 1
+             and cu_seqlens.numel() >= 1, "cu_seqlens must be [N + 1]")
+    _require(cu_seqlens.dtype in (torch.int32, torch.int64), "cu_seqlens must be int32 or int64")
+    N = cu_seqlens.numel() - 1
+    _check(cu_seqlens, "cu_seqlens", cu_seqlens.dtype, (N + 1,), dev)
+    _check(q, "q", torch.bfloat16, (T, h_qk, D), dev)
+    _check(k, "k", torch.bfloat16, (T, h_qk, D), dev)
+    _check(v, "v", torch.bfloat16, (T, h_v, D), dev)
+    _check(A_log, "A_log", torch.float32, (h_v,), dev)
+    _check(a, "a", torch.bfloat16, (T, h_v), dev)
+    _check(dt_bias, "dt_bias", torch.float32, (h_v,), dev)
+    _check(b, "b", torch.bfloat16, (T, h_v), dev)
+    _check(output, "output", torch.bfloat16, (T, h_v, D), dev)
+    _check(new_state, "new_state", torch.float32, (N, h_v, D, D), dev)
+    if state is not None:
+        _check(state, "state", torch.float32, (N, h_v, D, D), dev)
+    lib = _lib.load()
+    _lib.check(lib.gdn_b200_prefill(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
+        _ptr(cu_seqlens), 1 if cu_seqlens.dtype == torch.int64 else 0, float(scale or 0.0),
+        _ptr(output), _ptr(new_state), N, T, h_qk, h_v, D, _stream(dev)))
+
+
+def decode(q, k, v, state, A_log, a, dt_bias, b, scale: float = 0.0, *, in_place: bool = False):
+    """Allocating decode: returns ``(output, new_state)``; with ``in_place`` the
+    new state is written into ``state``."""
+    B, _, _, D = q.shape
+    h_v = v.shape[2]
+    output = torch.empty((B, 1, h_v, D), dtype=torch.bfloat16, device=q.device)
+    if in_place:
+        _require(state is not None, "in_place needs a state tensor")
+        new_state = state
+    else:
+        new_state = torch.empty((B, h_v, D, D), dtype=torch.float32, device=q.device)
+    gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+    return output, new_state
+
+
+def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale: float = 0.0, *,
+            in_place: bool = False):
+    """Allocating prefill: returns ``(output, new_state)``."""
+    T, _, D = q.shape
+    h_v = v.shape[1]
+    N = cu_seqlens.numel() - 1
+    output = torch.empty((T, h_v, D), dtype=torch.bfloat16, device=q.device)
+    if in_place:
+        _require(state is not None, "in_place needs a state tensor")
+        new_state = state
+    else:
+        new_state = torch.empty((N, h_v, D, D), dtype=torch.float32, device=q.device)
+    gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+    return output, new_state
+
+
+def load_tvm_kernel(kind: str):
+    """The TVM-FFI ``kernel`` function of this package for ``kind`` in
+    {"decode", "prefill"}: the object the reference's harness binds."""
+    import tvm_ffi
+
+    path = {"decode": _lib.TVM_DECODE_PATH, "prefill": _lib.TVM_PREFILL_PATH}[kind]
+    return tvm_ffi.load_module(path)["kernel"]

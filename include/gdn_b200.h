@@ -1,0 +1,89 @@
+/*
+ * gdn_b200.h — C ABI of the B200 (sm_100a) Gated DeltaNet hot path.
+ *
+ * Plain pointers and sizes; no framework types.  Every buffer is device
+ * memory owned by the caller (destination-passing style, outputs last), and
+ * no entry point allocates device memory or synchronises the stream: each
+ * call validates its arguments on the host, enqueues its kernel on `stream`
+ * (a cudaStream_t; NULL = the legacy default stream) and returns.
+ *
+ * Layouts (all contiguous, row-major, D = head_dim = 128):
+ *   decode : q, k [B,1,H_qk,D] bf16;  v [B,1,H_v,D] bf16;  a, b [B,1,H_v] bf16;
+ *            state, new_state [B,H_v,D(v),D(k)] fp32 (k-last);  output [B,1,H_v,D] bf16.
+ *   prefill: q, k [T,H_qk,D] bf16;  v [T,H_v,D] bf16;  a, b [T,H_v] bf16 (packed tokens);
+ *            cu_seqlens [N+1] int32 or int64;  state, new_state [N,H_v,D,D] fp32;
+ *            output [T,H_v,D] bf16.
+ *   A_log, dt_bias: [H_v] fp32.   H_v % H_qk == 0 (v-head h reads qk-head h / (H_v/H_qk)).
+ *
+ * Semantics (identical to the reference's TVM-FFI `kernel` entry points):
+ *   scale == 0      -> 1/sqrt(D)                               (ref solution/cuda/kernel.cu:115-118)
+ *   state == NULL   -> zero initial state                      (ref kernel.cu:135-139)
+ *   new_state may alias state (in-place update); output must not alias any input.
+ *   prefill: an empty sequence copies its initial state        (ref kernel_prefill.cu:61-66)
+ *
+ * Return value: GDN_B200_OK, or an error code whose message is available from
+ * gdn_b200_last_error() on the calling thread.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_B200_OK 0
+#define GDN_B200_ERR_INVALID_ARGUMENT 1  /* shape, pointer, alignment or head-layout error */
+#define GDN_B200_ERR_CUDA 2              /* a CUDA runtime/driver call failed */
+
+/* Device status bits (read with gdn_b200_device_status). */
+#define GDN_B200_STATUS_TMA_TIMEOUT 1u   /* a prefill TMA wait exceeded its bound */
+#define GDN_B200_STATUS_MMA_TIMEOUT 2u   /* a prefill tensor-core wait exceeded its bound */
+#define GDN_B200_STATUS_BAD_SEQLENS 4u   /* a cu_seqlens entry was outside [0, total_tokens] */
+
+/*
+ * One T=1 decode step for `batch` sequences.
+ * Replaces the reference's TVM-FFI `kernel` of solution/cuda/kernel.cu:101-150
+ * (GDNDecodeKernel(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)),
+ * with the tensor extents passed explicitly.
+ */
+int gdn_b200_decode(const void* q, const void* k, const void* v, const float* state,
+                    const float* A_log, const void* a, const float* dt_bias, const void* b,
+                    double scale, void* output, float* new_state,
+                    int64_t batch, int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                    void* stream);
+
+/*
+ * Chunked (C=64) prefill over `num_seqs` packed variable-length sequences.
+ * Replaces the reference's TVM-FFI `kernel` of solution/cuda/kernel_prefill.cu:300-339
+ * (GDNPrefillKernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+ * new_state)).  `cu_seqlens` is device memory of int32 (cu_seqlens_is_int64 = 0) or
+ * int64 (= 1) entries; `total_tokens` is the packed token extent T of q/k/v/a/b/output.
+ */
+int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* state,
+                     const float* A_log, const void* a, const float* dt_bias, const void* b,
+                     const void* cu_seqlens, int32_t cu_seqlens_is_int64, double scale,
+                     void* output, float* new_state,
+                     int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                     int32_t num_v_heads, int32_t head_dim, void* stream);
+
+/*
+ * Reads (and with clear != 0 resets) the status word that the kernels of
+ * this library set on `device` when a bounded device-side wait runs out or a
+ * cu_seqlens entry is out of range.  Synchronises the device.  No counterpart
+ * in the reference, which performs no device-side checks.
+ */
+int gdn_b200_device_status(int32_t device, uint32_t* status, int32_t clear);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* gdn_b200_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+int32_t gdn_b200_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif  /* GDN_B200_H_ */
