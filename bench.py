@@ -1,0 +1,491 @@
+"""Benchmark of the GDN hot path on B200 (one JSON line on stdout from rank 0).
+
+Headline (BASELINE metric, configs[1] at B=64): GDN decode, one T=1 step over
+B=64 sequences with qk16_v32 heads, fp32 state resident in HBM and updated in
+place.  ``value`` = state bytes moved per second (B * 32 * 128 * 128 * 4 * 2
+bytes per step) summed over ranks; ``ms_per_step`` = device time of one step.
+L2 is flushed between timed steps (see L2Flush), outside the timed events.
+
+Also reported on the same line:
+* ``prefill``: configs[2] (one 8192-token sequence, chunked C=64) tokens/s and
+  its tensor/HBM roofline, plus configs[3] (16 packed sequences) tokens/s;
+* ``decode_sweep``: configs[1] B in {1, 8, 32, 64, 128, 256};
+* ``roofline``: the decode kernel against the measured HBM copy bandwidth;
+* ``cpu_baseline``: the fp32 CPU oracle on the host cores (bounded sample);
+* ``e2e``: the decode metric through the C ABI with pinned host buffers,
+  host-to-device inputs and device-to-host output inside the timed region;
+* ``clocks``: nvidia-smi samples taken during the measurements.
+
+``--profile decode|prefill`` only launches a few kernels of one case (no timing,
+no output line): the command that the ncu summaries under profiles/ were made with.
+
+``--impl reference`` times the reference's algorithm on the host cores
+(the fp32 CPU restatement in oracle/, rank 0 only) for the same metric.
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs the same per-GPU
+workload on its own sequences and state shard (weak scaling, no collective on
+the data path); the step time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = ("GDN decode µs/step & HBM GB/s (B=64); chunked prefill tokens/s (T=8192)")
+UNIT = "GB/s"
+H_QK, H_V, D = 16, 32, 128
+STATE_BYTES_PER_SEQ = H_V * D * D * 4 * 2          # read + write of the fp32 state
+PREFILL_FLOP_PER_TOKEN_HEAD = 10 * 64 * D + 6 * D * D  # 180,224
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch recorded by an ncu capture summarised in profiles/."""
+    path = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s, p in zip(sm, power) if p > 1.2 * min(power)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
+                "samples": len(sm), "power_w_max": max(power), "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------------------- GPU arm
+class L2Flush:
+    """Evicts the timed kernel's data from L2 between timed steps: writes a
+    buffer of 2x the L2 size, then reads another buffer of 2x the L2 size so
+    that the L2 is left holding clean lines (no write-back of the flush's own
+    dirty lines is charged to the next timed kernel)."""
+
+    def __init__(self, l2_bytes):
+        n = max(256 << 20, 2 * l2_bytes) // 4
+        self.w = torch.empty(n, dtype=torch.float32, device="cuda")
+        self.r = torch.zeros(n, dtype=torch.float32, device="cuda")
+        self.sink = torch.empty((), dtype=torch.float32, device="cuda")
+
+    def zero_(self):
+        self.w.zero_()
+        torch.sum(self.r, dim=0, out=self.sink)
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def time_decode(K, batch, steps, warmup, flush, seed=0):
+    """Per-step device time (ms) of in-place decode steps; L2 flushed between steps."""
+    from gdn_kernel_b200 import workloads as W
+
+    x = W.make_decode_inputs(batch, seed=seed, device="cuda")
+    out = torch.empty(batch, 1, H_V, D, dtype=torch.bfloat16, device="cuda")
+    args = (x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.scale, out, x.state)
+    for _ in range(warmup):
+        flush.zero_()
+        K.gdn_decode(*args)
+    torch.cuda.synchronize()
+    ev = [_events() for _ in range(steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        K.gdn_decode(*args)
+        e1.record()
+    torch.cuda.synchronize()
+    times = [e0.elapsed_time(e1) for e0, e1 in ev]
+    del x, out
+    return times
+
+
+def time_decode_e2e(K, batch, steps, warmup, flush, seed=0):
+    """Decode through the C ABI with pinned host inputs/outputs each step."""
+    from gdn_kernel_b200 import workloads as W
+
+    x = W.make_decode_inputs(batch, seed=seed, device="cuda")
+    host_in = [t.cpu().pin_memory() for t in (x.q, x.k, x.v, x.a, x.b)]
+    dev_in = [t.clone() for t in (x.q, x.k, x.v, x.a, x.b)]
+    out = torch.empty(batch, 1, H_V, D, dtype=torch.bfloat16, device="cuda")
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def step():
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        q, k, v, a, b = dev_in
+        K.gdn_decode(q, k, v, x.state, x.A_log, a, x.dt_bias, b, x.scale, out, x.state)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    ev = [_events() for _ in range(steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        step()
+        e1.record()
+    torch.cuda.synchronize()
+    times = [e0.elapsed_time(e1) for e0, e1 in ev]
+    return times, h2d, d2h
+
+
+def time_prefill(K, lengths, iters, warmup, flush, seed=0, with_state=True):
+    from gdn_kernel_b200 import workloads as W
+
+    x = W.make_prefill_inputs(lengths, seed=seed, device="cuda", with_state=with_state)
+    T = sum(lengths)
+    out = torch.empty(T, H_V, D, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(len(lengths), H_V, D, D, dtype=torch.float32, device="cuda")
+    args = (x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale, out, ns)
+    for _ in range(warmup):
+        flush.zero_()
+        K.gdn_prefill(*args)
+    torch.cuda.synchronize()
+    ev = [_events() for _ in range(iters)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        K.gdn_prefill(*args)
+        e1.record()
+    torch.cuda.synchronize()
+    return [e0.elapsed_time(e1) for e0, e1 in ev]
+
+
+def prefill_hbm_bytes(lengths, with_state):
+    """Algorithmic HBM bytes of one prefill launch: q,k,v,a,b read, output written,
+    initial state read (if any) and final state written."""
+    T, N = sum(lengths), len(lengths)
+    tok = T * (2 * H_QK * D * 2 + H_V * D * 2 + 2 * H_V * 2)
+    out = T * H_V * D * 2
+    st = N * H_V * D * D * 4 * (2 if with_state else 1)
+    return tok + out + st
+
+
+def cpu_decode_sample(batch, steps, seed=0):
+    """The CPU oracle's decode on the host cores: seconds per step."""
+    from gdn_kernel_b200 import workloads as W
+    from oracle import gdn_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x = W.make_decode_inputs(batch, seed=seed)
+    state = x.state
+    O.decode_step(x.q, x.k, x.v, state, x.A_log, x.a, x.dt_bias, x.b, x.scale)  # warm
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _, state = O.decode_step(x.q, x.k, x.v, state, x.A_log, x.a, x.dt_bias, x.b, x.scale)
+    return (time.perf_counter() - t0) / steps
+
+
+def run_gpu(args, rank, world, local_rank):
+    import torch.distributed as dist
+
+    from gdn_kernel_b200 import _lib, kernel as K
+
+    torch.cuda.set_device(local_rank)
+    _lib.load()
+    peaks, peaks_src = load_peaks()
+    hbm_peak = float(peaks["hbm_gbs"])
+    tc_peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    l2 = torch.cuda.get_device_properties(local_rank).L2_cache_size
+    flush = L2Flush(l2)
+    B = args.batch
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+
+    # ---- headline: decode B=64, K timed steps
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    times = time_decode(K, B, args.steps, args.warmup, flush, seed=1000 + rank)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = sum(times)
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    step_bytes = B * STATE_BYTES_PER_SEQ
+    value = world * step_bytes * args.steps / (total_ms * 1e-3) / 1e9
+    mean_launch_ms = statistics.mean(times)
+    achieved = step_bytes / (mean_launch_ms * 1e-3) / 1e9
+
+    # ---- e2e through the C ABI with host buffers
+    e2e_times, h2d, d2h = time_decode_e2e(K, B, max(args.steps // 2, 10), args.warmup, flush,
+                                          seed=2000 + rank)
+    e2e_ms = sum(e2e_times)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * step_bytes * len(e2e_times) / (float(t.item()) * 1e-3) / 1e9
+
+    extra = {}
+    if not args.quick:
+        # ---- decode sweep
+        sweep = {}
+        for b in (1, 8, 32, 64, 128, 256):
+            ts = time_decode(K, b, 30, 3, flush, seed=3000 + b)
+            ms = statistics.median(ts)
+            sweep[str(b)] = {"us_per_step": round(ms * 1e3, 2),
+                             "state_GBps": round(b * STATE_BYTES_PER_SEQ / (ms * 1e-3) / 1e9, 1),
+                             "frac_hbm": round(b * STATE_BYTES_PER_SEQ / (ms * 1e-3) / 1e9
+                                               / hbm_peak, 3)}
+        extra["decode_sweep"] = sweep
+        # ---- prefill configs[2] and configs[3]
+        from gdn_kernel_b200 import workloads as W
+        pre = {}
+        for name, lengths, with_state in (
+                ("T8192", [8192], False),
+                ("varlen16", W.varlen_lengths(16, 128, 8192, seed=3), True)):
+            ts = time_prefill(K, lengths, 5, 2, flush, seed=4000 + rank, with_state=with_state)
+            ms = statistics.median(ts)
+            T = sum(lengths)
+            flop = T * H_V * PREFILL_FLOP_PER_TOKEN_HEAD
+            hb = prefill_hbm_bytes(lengths, with_state)
+            pre[name] = {
+                "tokens": T, "sequences": len(lengths), "us": round(ms * 1e3, 1),
+                "tokens_per_s": round(world * T / (ms * 1e-3), 1),
+                "tflops": round(flop / (ms * 1e-3) / 1e12, 2),
+                "tensor_frac": round(flop / (ms * 1e-3) / 1e12 / tc_peak, 4),
+                "hbm_GBps": round(hb / (ms * 1e-3) / 1e9, 1),
+                "hbm_frac": round(hb / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+                "algorithmic_flop": flop, "algorithmic_bytes": hb,
+            }
+        extra["prefill"] = pre
+
+    clocks = sampler.stop()
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            steps_cpu = args.cpu_steps
+            sec = cpu_decode_sample(B, steps_cpu)
+            cpu = {"value": round(step_bytes / sec / 1e9, 3), "unit": UNIT,
+                   "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"decode B={B} qk16_v32, {steps_cpu} steps of the fp32 CPU oracle "
+                             f"(torch, {torch.get_num_threads()} threads); "
+                             f"{sec * 1e3:.1f} ms/step"}
+        traffic = profile_traffic("decode_B64.md")
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "us_per_step": round(ms_per_step * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"decode B={B} per GPU, qk16_v32, D=128, T=1, in-place fp32 "
+                                   f"state (BASELINE configs[1] at B={B})",
+                       "batch_per_gpu": B, "num_qk_heads": H_QK, "num_v_heads": H_V,
+                       "head_dim": D, "l2": "flushed between timed steps (write 2x L2, then read 2x L2)",
+                       "parallelism": f"sequence-sharded x{world}, no collective"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "traffic": (traffic * 1.0 if traffic else None),
+                         "peak_source": f"{peaks_src} hbm_gbs (STREAM-style copy)",
+                         "kernel": "gdn_decode_kernel",
+                         "algorithmic_bytes_per_launch": step_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "path": "gdn_kernel_b200.gdn_decode -> libgdn_b200.so gdn_b200_decode, "
+                            "pinned host q/k/v/a/b in, output out; state resident in HBM"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        line.update(extra)
+    return line
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    """The reference's algorithm on the host cores (fp32 CPU restatement; the
+    reference's own code path is CUDA-only, so the port stands in)."""
+    B = args.batch
+    steps = max(1, min(args.steps, args.cpu_steps))
+    for _ in range(min(args.warmup, 1)):
+        cpu_decode_sample(B, 1, seed=7)
+    sec = cpu_decode_sample(B, steps)
+    step_bytes = B * STATE_BYTES_PER_SEQ
+    value = step_bytes / sec / 1e9
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"decode B={B}, qk16_v32, D=128, T=1 (BASELINE configs[1] at "
+                               f"B={B}) on the host cores", "batch_per_gpu": B},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"{steps} decode steps at B={B} of the fp32 CPU oracle "
+                                   f"(torch, {torch.get_num_threads()} threads)"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_profile(args):
+    """A handful of launches of one case, for ncu captures."""
+    from gdn_kernel_b200 import _lib, kernel as K, workloads as W
+
+    torch.cuda.set_device(0)
+    _lib.load()
+    if args.profile == "decode":
+        x = W.make_decode_inputs(args.batch, seed=0, device="cuda")
+        out = torch.empty(args.batch, 1, H_V, D, dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.launches):
+            K.gdn_decode(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.scale, out,
+                         x.state)
+    else:
+        lengths = ([args.tokens] if args.sequences == 1
+                   else W.varlen_lengths(args.sequences, 128, args.tokens, seed=3))
+        x = W.make_prefill_inputs(lengths, seed=0, device="cuda", with_state=args.sequences > 1)
+        out = torch.empty(sum(lengths), H_V, D, dtype=torch.bfloat16, device="cuda")
+        ns = torch.empty(len(lengths), H_V, D, D, dtype=torch.float32, device="cuda")
+        for _ in range(args.launches):
+            K.gdn_prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
+                          x.scale, out, ns)
+    torch.cuda.synchronize()
+    assert _lib.device_status(0) == 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-steps", type=int, default=20)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="headline decode + e2e only")
+    ap.add_argument("--profile", choices=["decode", "prefill"], default=None)
+    ap.add_argument("--launches", type=int, default=4)
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--sequences", type=int, default=1)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.profile:
+        run_profile(args)
+        return
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_gpu(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -8,12 +8,12 @@
 //   s = g S_v;  delta_v = beta (v_v - <s,k>);  S_v' = s + delta_v k;
 //   o_v = scale (<s,q> + delta_v <k,q>)
 //
-// Layout on the SM: one CTA of 4 warps per (batch, v-head) = 64 KiB of state.
-// Eight lanes share one 512-byte state row (each lane holds four float4 at
-// columns 4*l8 + 32*j), so one warp instruction moves four full rows, fully
-// coalesced, and the two row reductions are 3-level xor shuffles.  Each warp
-// streams 32 rows with a three-deep register pipeline (loads for iteration
-// it+2 are in flight while iteration it is reduced and written back in place).
+// Layout on the SM: a CTA of 4 warps covers kRowsPerCta = 16 * kIters rows of
+// one (batch, v-head) state.  Eight lanes share one 512-byte state row (each
+// lane holds four float4 at columns 4*l8 + 32*j), so one warp instruction moves
+// four full rows, fully coalesced, and the two row reductions are 3-level xor
+// shuffles.  Each warp streams 4 * kIters rows through a register pipeline
+// kPipe iterations deep, writing every row back in place.
 #pragma once
 
 #include "gdn_ptx.cuh"
@@ -22,7 +22,20 @@ namespace gdn {
 
 constexpr int kHeadDim = 128;
 constexpr int kDecodeThreads = 128;
-constexpr int kDecodeIters = 8;  // 4 rows per warp per iteration, 32 rows per warp
+#ifndef GDN_DECODE_ITERS
+#define GDN_DECODE_ITERS 1   // 4 rows per warp per iteration
+#endif
+#ifndef GDN_DECODE_PIPE
+#define GDN_DECODE_PIPE 1    // iterations of loads in flight ahead of the reduction
+#endif
+#ifndef GDN_DECODE_LDHINT
+#define GDN_DECODE_LDHINT 1  // L1::no_allocate + L2::256B prefetch on state loads
+#endif
+constexpr int kDecodeIters = GDN_DECODE_ITERS;
+constexpr int kDecodePipe = GDN_DECODE_PIPE;
+constexpr int kDecodeRowsPerCta = 16 * kDecodeIters;
+constexpr int kDecodeCtasPerHead = kHeadDim / kDecodeRowsPerCta;
+static_assert(kHeadDim % kDecodeRowsPerCta == 0, "rows per CTA must divide 128");
 
 struct DecodeParams {
   const __nv_bfloat16* q;        // [B, 1, H_qk, K]
@@ -46,9 +59,15 @@ __device__ __forceinline__ float softplus20(float x) {
 
 __device__ __forceinline__ float4 ld_state(const float* p) {
   float4 r;
+#if GDN_DECODE_LDHINT
   asm volatile("ld.global.L1::no_allocate.L2::256B.v4.f32 {%0,%1,%2,%3}, [%4];"
                : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
                : "l"(p));
+#else
+  asm volatile("ld.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+#endif
   return r;
 }
 
@@ -68,7 +87,11 @@ __device__ __forceinline__ void load_bf16x4(const __nv_bfloat16* p, float* dst) 
 
 template <bool kHasState>
 __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams p) {
-  const int bh = blockIdx.x;                 // batch * H_v + v-head
+  constexpr int kIters = kDecodeIters;
+  constexpr int kPipe = kDecodePipe < kDecodeIters ? kDecodePipe : kDecodeIters;
+  constexpr int kBuf = kPipe < kDecodeIters ? kPipe + 1 : kDecodeIters;
+  const int bh = blockIdx.x / kDecodeCtasPerHead;   // batch * H_v + v-head
+  const int rblk = blockIdx.x % kDecodeCtasPerHead;
   const int h = bh % p.h_v;
   const int bidx = bh / p.h_v;
   const int hq = h / (p.h_v / p.h_qk);       // GQA: v-head h reads qk-head h / (H_v/H_qk)
@@ -76,6 +99,24 @@ __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams
   const int lane = threadIdx.x & 31;
   const int sub = lane >> 3;                 // row inside the warp's 4-row group
   const int l8 = lane & 7;                   // column slot inside the row
+
+  // State loads first: they are independent of the gate and q/k loads and
+  // carry the DRAM latency that everything else overlaps with.
+  const size_t sbase = static_cast<size_t>(bh) * kHeadDim * kHeadDim;
+  // iteration it touches row row0 + 4*it
+  const int row0 = rblk * kDecodeRowsPerCta + warp * (4 * kIters) + sub;
+  const float* src = kHasState ? p.state + sbase + static_cast<size_t>(row0) * kHeadDim + 4 * l8
+                               : nullptr;
+  float* dst = p.new_state + sbase + static_cast<size_t>(row0) * kHeadDim + 4 * l8;
+  const __nv_bfloat16* vrow = p.v + static_cast<size_t>(bh) * kHeadDim;
+
+  float4 buf[kBuf][4];
+  if (kHasState) {
+#pragma unroll
+    for (int it = 0; it < kPipe; ++it)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) buf[it % kBuf][j] = ld_state(src + it * 4 * kHeadDim + 32 * j);
+  }
 
   // Gate and beta for this (batch, v-head) (ref kernel.cu:44-53).
   const float av = __bfloat162float(p.a[bh]);
@@ -98,34 +139,19 @@ __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams
   qk += __shfl_xor_sync(0xffffffffu, qk, 2);
   qk += __shfl_xor_sync(0xffffffffu, qk, 4);
 
-  const size_t sbase = static_cast<size_t>(bh) * kHeadDim * kHeadDim;
-  const int row0 = warp * (4 * kDecodeIters) + sub;  // iteration it touches row0 + 4*it
-  const float* src = kHasState ? p.state + sbase + static_cast<size_t>(row0) * kHeadDim + 4 * l8
-                               : nullptr;
-  float* dst = p.new_state + sbase + static_cast<size_t>(row0) * kHeadDim + 4 * l8;
-  const __nv_bfloat16* vrow = p.v + static_cast<size_t>(bh) * kHeadDim;
-
-  float4 buf[3][4];
-  if (kHasState) {
+  float outv[kIters];
 #pragma unroll
-    for (int it = 0; it < 2; ++it)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) buf[it][j] = ld_state(src + it * 4 * kHeadDim + 32 * j);
-  }
-
-  float outv[kDecodeIters];
-#pragma unroll
-  for (int it = 0; it < kDecodeIters; ++it) {
-    if (kHasState && it + 2 < kDecodeIters) {
+  for (int it = 0; it < kIters; ++it) {
+    if (kHasState && it + kPipe < kIters) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        buf[(it + 2) % 3][j] = ld_state(src + (it + 2) * 4 * kHeadDim + 32 * j);
+        buf[(it + kPipe) % kBuf][j] = ld_state(src + (it + kPipe) * 4 * kHeadDim + 32 * j);
     }
     float s[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (kHasState) {
-        const float4 x = buf[it % 3][j];
+        const float4 x = buf[it % kBuf][j];
         s[4 * j + 0] = g * x.x; s[4 * j + 1] = g * x.y;
         s[4 * j + 2] = g * x.z; s[4 * j + 3] = g * x.w;
       } else {
@@ -159,7 +185,7 @@ __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams
   if (l8 == 0) {
     __nv_bfloat16* orow = p.out + static_cast<size_t>(bh) * kHeadDim;
 #pragma unroll
-    for (int it = 0; it < kDecodeIters; ++it) orow[row0 + 4 * it] = __float2bfloat16(outv[it]);
+    for (int it = 0; it < kIters; ++it) orow[row0 + 4 * it] = __float2bfloat16(outv[it]);
   }
 }
 

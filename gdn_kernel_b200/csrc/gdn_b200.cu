@@ -129,7 +129,7 @@ extern "C" int gdn_b200_decode(const void* q, const void* k, const void* v, cons
   t_last_error.clear();
   if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
   if (batch < 0) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch must be >= 0");
-  if (batch * num_v_heads > 0x7fffffffLL)
+  if (batch * num_v_heads * kDecodeCtasPerHead > 0x7fffffffLL)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch * num_v_heads exceeds the grid limit");
   if (batch == 0) return GDN_B200_OK;
   if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !new_state)
@@ -154,7 +154,7 @@ extern "C" int gdn_b200_decode(const void* q, const void* k, const void* v, cons
   p.new_state = new_state;
   p.h_qk = num_qk_heads;
   p.h_v = num_v_heads;
-  const dim3 grid(static_cast<unsigned>(batch * num_v_heads));
+  const dim3 grid(static_cast<unsigned>(batch * num_v_heads * kDecodeCtasPerHead));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (state)
     gdn_decode_kernel<true><<<grid, kDecodeThreads, 0, st>>>(p);
