@@ -238,6 +238,50 @@ def time_prefill(K, lengths, iters, warmup, flush, seed=0, with_state=True):
     return [e0.elapsed_time(e1) for e0, e1 in ev]
 
 
+def _max_over_ranks(ms, world):
+    if world == 1:
+        return ms
+    import torch.distributed as dist
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_sharded(K, rank, world, flush, hbm_peak):
+    """a fixed whole-box workload partitioned by sequence
+    (strong scaling): (a) decode B=1024 as contiguous batch blocks; (b) packed
+    prefill of 64 sequences with lengths U[1024, 16384], LPT-assigned."""
+    from gdn_kernel_b200 import sharding as S, workloads as W
+    import torch.distributed as dist
+
+    res = {}
+    lo, hi = S.decode_shards(1024, world)[rank]
+    if world > 1:
+        dist.barrier()
+    ts = time_decode(K, hi - lo, 20, 3, flush, seed=5000 + rank)
+    ms = _max_over_ranks(statistics.median(ts), world)
+    step_bytes = 1024 * STATE_BYTES_PER_SEQ
+    gbps = step_bytes / (ms * 1e-3) / 1e9
+    res["decode_B1024"] = {"us_per_step": round(ms * 1e3, 2), "state_GBps": round(gbps, 1),
+                           "per_gpu_frac_hbm": round(gbps / world / hbm_peak, 4),
+                           "box_frac_hbm": round(gbps / (world * hbm_peak), 4),
+                           "batch_per_gpu": hi - lo}
+    lengths = W.varlen_lengths(64, 1024, 16384, seed=4)
+    mine = [lengths[i] for i in S.prefill_shards(lengths, world)[rank]]
+    if world > 1:
+        dist.barrier()
+    pts = time_prefill(K, mine, 3, 2, flush, seed=6000 + rank) if mine else [0.0]
+    pms = _max_over_ranks(statistics.median(pts), world)
+    T = sum(lengths)
+    hb = prefill_hbm_bytes(lengths, True)
+    res["prefill_64seq"] = {"tokens": T, "us": round(pms * 1e3, 1),
+                            "tokens_per_s": round(T / (pms * 1e-3), 1),
+                            "hbm_GBps": round(hb / (pms * 1e-3) / 1e9, 1),
+                            "box_frac_hbm": round(hb / (pms * 1e-3) / 1e9 / (world * hbm_peak), 4),
+                            "tokens_this_rank": sum(mine)}
+    return res
+
+
 def prefill_hbm_bytes(lengths, with_state):
     """Algorithmic HBM bytes of one prefill launch: q,k,v,a,b read, output written,
     initial state read (if any) and final state written."""
@@ -342,6 +386,7 @@ def run_gpu(args, rank, world, local_rank):
                 "algorithmic_flop": flop, "algorithmic_bytes": hb,
             }
         extra["prefill"] = pre
+        extra["sharded"] = run_sharded(K, rank, world, flush, hbm_peak)
 
     clocks = sampler.stop()
 

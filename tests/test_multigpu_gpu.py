@@ -1,0 +1,41 @@
+"""Sequence-sharded runs on 2 GPUs (one process each) equal the single-GPU run
+bitwise: every CTA of both kernels touches one sequence only."""
+
+import pytest
+import torch
+
+import dist_workers as DW
+from gdn_kernel_b200 import kernel as K, sharding as S, workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def _need_two():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+
+
+def test_two_gpu_prefill_equals_one_gpu():
+    _need_two()
+    res = S.launch_workers(DW.gpu_prefill_worker, 2, 29711, timeout_s=300)
+    assert all(r.ok for r in res), [r.error for r in res]
+    out, ns = res[0].value
+    x = W.make_prefill_inputs(DW.PREFILL_LENGTHS, seed=77, h_qk=2, h_v=4, device="cuda")
+    ro, rs = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
+                       x.scale)
+    assert torch.equal(out, ro.cpu()) and torch.equal(ns, rs.cpu())
+
+
+def test_two_gpu_decode_equals_one_gpu():
+    _need_two()
+    res = S.launch_workers(DW.gpu_decode_worker, 2, 29712, timeout_s=300)
+    assert all(r.ok for r in res), [r.error for r in res]
+    outs, state = res[0].value
+    first, tokens = W.make_decode_run(DW.DECODE_BATCH, 3, seed=12, h_qk=2, h_v=4)
+    st = first.state.cuda()
+    ref = []
+    for (q, k, v, a, b) in tokens:
+        o, _ = K.decode(q.cuda(), k.cuda(), v.cuda(), st, first.A_log.cuda(), a.cuda(),
+                        first.dt_bias.cuda(), b.cuda(), first.scale, in_place=True)
+        ref.append(o.cpu())
+    assert torch.equal(outs, torch.stack(ref)) and torch.equal(state, st.cpu())
