@@ -186,7 +186,15 @@ def _worker_main(fn, rank, world, port, backend, result_q, pg_timeout_s):
             pass
 
 
-def launch_workers(fn: Callable[[int, int], object], world: int, port: int,
+def free_port() -> int:
+    """A TCP port on 127.0.0.1 that is free right now (for the rendezvous store)."""
+    import socket
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def launch_workers(fn: Callable[[int, int], object], world: int, port: Optional[int] = None,
                    backend: str = "gloo", timeout_s: float = 120.0,
                    pg_timeout_s: float = 30.0) -> List[WorkerResult]:
     """Run ``fn(rank, world)`` in ``world`` spawned processes joined by a process
@@ -194,6 +202,8 @@ def launch_workers(fn: Callable[[int, int], object], world: int, port: int,
     with its traceback; a rank that neither reports nor exits within
     ``timeout_s`` is terminated and reported as failed.  ``fn`` must be
     picklable (a module-level function)."""
+    if port is None:
+        port = free_port()
     ctx = mp.get_context("spawn")
     result_q = ctx.Queue()
     procs = [ctx.Process(target=_worker_main,

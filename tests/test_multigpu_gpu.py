@@ -17,7 +17,7 @@ def _need_two():
 
 def test_two_gpu_prefill_equals_one_gpu():
     _need_two()
-    res = S.launch_workers(DW.gpu_prefill_worker, 2, 29711, timeout_s=300)
+    res = S.launch_workers(DW.gpu_prefill_worker, 2, timeout_s=300)
     assert all(r.ok for r in res), [r.error for r in res]
     out, ns = res[0].value
     x = W.make_prefill_inputs(DW.PREFILL_LENGTHS, seed=77, h_qk=2, h_v=4, device="cuda")
@@ -28,7 +28,7 @@ def test_two_gpu_prefill_equals_one_gpu():
 
 def test_two_gpu_decode_equals_one_gpu():
     _need_two()
-    res = S.launch_workers(DW.gpu_decode_worker, 2, 29712, timeout_s=300)
+    res = S.launch_workers(DW.gpu_decode_worker, 2, timeout_s=300)
     assert all(r.ok for r in res), [r.error for r in res]
     outs, state = res[0].value
     first, tokens = W.make_decode_run(DW.DECODE_BATCH, 3, seed=12, h_qk=2, h_v=4)

@@ -10,8 +10,6 @@ import dist_workers as DW
 from gdn_kernel_b200 import sharding as S, workloads as W
 from oracle import gdn_oracle as O
 
-PORT = 29611
-
 
 def test_decode_shards_cover_contiguously():
     for batch in (0, 1, 7, 64, 1024, 1023):
@@ -51,7 +49,7 @@ def test_pack_and_scatter_roundtrip():
 
 
 def test_two_rank_prefill_matches_single_process():
-    res = S.launch_workers(DW.sharded_prefill_worker, 2, PORT)
+    res = S.launch_workers(DW.sharded_prefill_worker, 2)
     assert all(r.ok for r in res), [r.error for r in res]
     out, ns = res[0].value
     x = W.make_prefill_inputs(DW.PREFILL_LENGTHS, seed=77, h_qk=2, h_v=4)
@@ -62,7 +60,7 @@ def test_two_rank_prefill_matches_single_process():
 
 
 def test_two_rank_decode_matches_single_process():
-    res = S.launch_workers(DW.sharded_decode_worker, 2, PORT + 1)
+    res = S.launch_workers(DW.sharded_decode_worker, 2)
     assert all(r.ok for r in res), [r.error for r in res]
     outs, state = res[0].value
     first, tokens = W.make_decode_run(DW.DECODE_BATCH, 3, seed=12, h_qk=2, h_v=4)
@@ -76,19 +74,19 @@ def test_two_rank_decode_matches_single_process():
 
 
 def test_failed_rank_is_reported_and_others_finish():
-    res = S.launch_workers(DW.failing_worker, 2, PORT + 2)
+    res = S.launch_workers(DW.failing_worker, 2)
     assert res[0].ok and res[0].value == "rank0 done"
     assert not res[1].ok and "injected failure on rank 1" in res[1].error
 
 
 def test_peer_failure_ends_collective_with_error_not_hang():
-    res = S.launch_workers(DW.failing_before_barrier_worker, 2, PORT + 3, timeout_s=90,
+    res = S.launch_workers(DW.failing_before_barrier_worker, 2, timeout_s=90,
                            pg_timeout_s=5)
     assert not res[1].ok and "injected failure" in res[1].error
     assert not res[0].ok        # its barrier failed instead of waiting forever
 
 
 def test_silent_rank_is_terminated_at_the_deadline():
-    res = S.launch_workers(DW.silent_worker, 2, PORT + 4, timeout_s=20)
+    res = S.launch_workers(DW.silent_worker, 2, timeout_s=20)
     assert res[0].ok and res[0].value == 0
     assert not res[1].ok and "did not report" in res[1].error
