@@ -25,10 +25,16 @@
 //   D_S4 [128x128] = K^T (v_new e^{gamma_last-gamma})   (S^T increment)
 // The fp32 state lives in registers of the 256 threads (thread = TMEM lane k,
 // column half), its bf16 copy is the MN-major B operand of the S^T products.
-// The 64x64 triangular inverse runs in fp32 on CUDA cores (blocked 16x16).
+// The 64x64 triangular inverse runs in fp32 on CUDA cores (blocked: 16x16
+// diagonal inverses, 16-level merges, one 32-level merge).
+//
+// Pipelining: the next chunk's tiles are requested as soon as the buffer they
+// land in has been consumed (V after the U product, Q and K after the S^T
+// product, the K tile after the state-increment product), and the next chunk's
+// gates are computed by a warp that is idle during the v_new epilogue.
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records a status bit,
-// stops, frees its TMEM and returns.
+// stops at the end of the chunk, frees its TMEM and returns.
 #pragma once
 
 #include <cuda.h>
@@ -48,15 +54,13 @@ constexpr uint32_t kOffTPZT = kOffVB + 16384;      // 32 KiB: T' | P | Z | T_b, 
 constexpr uint32_t kOffSB = kOffTPZT + 32768;      // 32 KiB: S^T bf16 [kd][v], v-blocks of 16 KiB
 constexpr uint32_t kOffVN = kOffSB + 32768;        // 16 KiB: v_new [c][v]
 constexpr uint32_t kOffVND = kOffVN + 16384;       // 16 KiB: v_new e^{gamma_last-gamma_c}
-constexpr int kLdA = 65;                           // fp32 row pitch of A and T
-constexpr uint32_t kOffAF = kOffVND + 16384;       // fp32 A [64][65]
-constexpr uint32_t kOffTF = kOffAF + 64 * kLdA * 4;  // fp32 T [64][65]
-constexpr uint32_t kOffXS = kOffTF + 64 * kLdA * 4;  // fp32 scratch, 3 blocks of 16x16
-constexpr uint32_t kOffGam = kOffXS + 3 * 256 * 4;   // gamma[64]
-constexpr uint32_t kOffBeta = kOffGam + 256;         // beta[64]
-constexpr uint32_t kOffEG = kOffBeta + 256;          // e^gamma[64]
-constexpr uint32_t kOffBar = kOffEG + 256;           // 2 mbarriers
-constexpr uint32_t kOffTmemPtr = kOffBar + 16;
+constexpr int kLdA = 68;                           // fp32 row pitch of A and T (16-byte rows)
+constexpr uint32_t kOffAF = kOffVND + 16384;       // fp32 A [64][68]
+constexpr uint32_t kOffTF = kOffAF + 64 * kLdA * 4;  // fp32 T [64][68]
+constexpr uint32_t kOffXS = kOffTF + 64 * kLdA * 4;  // fp32 scratch of the solve, 32x40
+constexpr uint32_t kOffGate = kOffXS + 32 * 40 * 4;  // 2 buffers x {gamma, beta, e^gamma}[64]
+constexpr uint32_t kOffBar = kOffGate + 2 * 3 * 256; // 5 mbarriers
+constexpr uint32_t kOffTmemPtr = kOffBar + 48;
 constexpr uint32_t kSmemUsed = kOffTmemPtr + 16;
 constexpr uint32_t kPrefillSmem = kSmemUsed + 1024;  // slack to align the base
 
@@ -67,7 +71,7 @@ constexpr uint32_t kTmUO = 192;
 constexpr uint32_t kTmS4 = 320;
 constexpr uint32_t kTmCols = 512;
 
-constexpr uint32_t kTmaBytesPerChunk = 8 * 8192;   // Q, K (twice), V: 2 boxes each
+constexpr uint32_t kTileBytes = 8192;              // one 64 x 64 bf16 TMA box
 
 struct PrefillParams {
   const float* state;            // [N, H_v, V, K] or nullptr (zero state)
@@ -95,21 +99,8 @@ __device__ __forceinline__ long long load_cu(const PrefillParams& p, int i) {
                        : static_cast<long long>(reinterpret_cast<const int*>(p.cu_seqlens)[i]);
 }
 
-// Store 64 fp32 values as one 128-byte bf16 row of a 128B-swizzled tile.
-__device__ __forceinline__ void st_row_bf16(uint8_t* tile, uint32_t row, const float* x,
-                                            float mul) {
-#pragma unroll
-  for (int cc = 0; cc < 8; ++cc) {
-    uint4 u;
-    u.x = pack_bf16x2(x[8 * cc + 0] * mul, x[8 * cc + 1] * mul);
-    u.y = pack_bf16x2(x[8 * cc + 2] * mul, x[8 * cc + 3] * mul);
-    u.z = pack_bf16x2(x[8 * cc + 4] * mul, x[8 * cc + 5] * mul);
-    u.w = pack_bf16x2(x[8 * cc + 6] * mul, x[8 * cc + 7] * mul);
-    *reinterpret_cast<uint4*>(tile + sw128_off(row, cc)) = u;
-  }
-}
-
-// Store 32 fp32 values as half (chunks c0..c0+3) of a 128-byte bf16 row.
+// Store 32 fp32 values as chunks c0..c0+3 of a 128-byte bf16 row of a
+// 128B-swizzled tile.
 __device__ __forceinline__ void st_half_row_bf16(uint8_t* tile, uint32_t row, uint32_t c0,
                                                  const float* x, float mul) {
 #pragma unroll
@@ -123,52 +114,231 @@ __device__ __forceinline__ void st_half_row_bf16(uint8_t* tile, uint32_t row, ui
   }
 }
 
-// T = (I - A)^{-1} for the strictly lower 64x64 fp32 A, blocked in 16x16:
-//   T_ii = (I - A_ii)^{-1}                  (forward substitution per column)
-//   T_ij = T_ii sum_{k=j}^{i-1} A_ik T_kj  (i > j, by block diagonals)
-// Only the lower triangle (including the unit diagonal) of T is written.
-__device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float* X, int tid) {
-  if (tid < 64) {
-    const int blk = tid >> 4, j = tid & 15, o = 16 * blk;
-    float x[16];
+__device__ __forceinline__ void st_row_bf16(uint8_t* tile, uint32_t row, const float* x) {
+  st_half_row_bf16(tile, row, 0, x, 1.0f);
+  st_half_row_bf16(tile, row, 4, x + 32, 1.0f);
+}
+
+__device__ __forceinline__ void zero_half_row(uint8_t* tile, uint32_t row, uint32_t c0) {
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
+  for (int cc = 0; cc < 4; ++cc)
+    *reinterpret_cast<uint4*>(tile + sw128_off(row, c0 + cc)) = make_uint4(0, 0, 0, 0);
+}
+
+// Two 32-column TMEM loads in flight, then one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&r)[64]) {
+  tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(r));
+  tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(r + 32));
+  tmem_wait_ld();
+}
+
+// ---------------------------------------------------------------- triangular inverse
+// 3xTF32 tensor-core products: x = x_hi + x_lo with both halves tf32, and
+// a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi accumulated in fp32, which keeps the
+// products at fp32-level accuracy.
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// One 16x8 tile of D = L * R (L: 16 x 8*KSTEPS rows of pitch ldl; R: 8*KSTEPS x 8
+// of pitch ldr), one warp.  Lane (g = lane/4, t = lane%4) receives
+// D[g][2t], D[g][2t+1], D[g+8][2t], D[g+8][2t+1].
+template <int KSTEPS>
+__device__ __forceinline__ void mma_tile_3xtf32(float (&d)[4], const float* L, int ldl,
+                                                const float* R, int ldr, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  d[0] = d[1] = d[2] = d[3] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks) {
+    const float av[4] = {L[g * ldl + 8 * ks + t], L[(g + 8) * ldl + 8 * ks + t],
+                         L[g * ldl + 8 * ks + t + 4], L[(g + 8) * ldl + 8 * ks + t + 4]};
+    const float bv[2] = {R[(8 * ks + t) * ldr + g], R[(8 * ks + t + 4) * ldr + g]};
+    uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      ah[e] = to_tf32(av[e]);
+      al[e] = to_tf32(av[e] - __uint_as_float(ah[e]));
+    }
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      bh[e] = to_tf32(bv[e]);
+      bl[e] = to_tf32(bv[e] - __uint_as_float(bh[e]));
+    }
+    mma_tf32(d, al, bh);
+    mma_tf32(d, ah, bl);
+    mma_tf32(d, ah, bh);
+  }
+}
+
+// T'[i][j] = T[i][j] beta_j e^{gamma_j} and T_b[i][j] = T[i][j] beta_j, as bf16
+// into the K-major swizzled tiles T' (TPZT + 0) and T_b (TPZT + 24 KiB).
+__device__ __forceinline__ void st_tp_one(uint8_t* smem, int i, int j, float t, const float* bet,
+                                          const float* eg) {
+  const uint32_t off = sw128_off(i, j >> 3) + (j & 7) * 2;
+  const float tb = t * bet[j];
+  *reinterpret_cast<__nv_bfloat16*>(smem + kOffTPZT + 24576 + off) = __float2bfloat16(tb);
+  *reinterpret_cast<__nv_bfloat16*>(smem + kOffTPZT + off) = __float2bfloat16(tb * eg[j]);
+}
+
+__device__ __forceinline__ void st_tp_pair(uint8_t* smem, int i, int j, float t0, float t1,
+                                           const float* bet, const float* eg) {
+  const uint32_t off = sw128_off(i, j >> 3) + (j & 7) * 2;   // j even: 4-byte aligned pair
+  const float b0 = t0 * bet[j], b1 = t1 * bet[j + 1];
+  *reinterpret_cast<uint32_t*>(smem + kOffTPZT + 24576 + off) = pack_bf16x2(b0, b1);
+  *reinterpret_cast<uint32_t*>(smem + kOffTPZT + off) = pack_bf16x2(b0 * eg[j], b1 * eg[j + 1]);
+}
+
+// T = (I - A)^{-1} for the strictly lower 64x64 fp32 A (row pitch kLdA), by
+// block doubling; every level is one or two barrier-separated steps:
+//   1. T_bb = (I - A_bb)^{-1} for the eight 8x8 diagonal blocks (forward
+//      substitution, one column per thread, CUDA cores);
+//   2. 8 -> 16:  T_hl = T_hh (A_hl T_ll) for the four 8x8 sub-diagonal blocks;
+//   3. 16 -> 32: the same for the two 16x16 sub-diagonal blocks (3xTF32 mma);
+//   4. 32 -> 64: the same for the 32x32 lower-left block (3xTF32 mma).
+// Results go to T (fp32, read by the next level) and straight into the bf16
+// T' / T_b operand tiles.  T's strictly-upper 8x8 blocks and the upper parts of
+// the T' / T_b tiles are zeroed once per CTA and never written.
+__device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float* X, uint8_t* smem,
+                                                 const float* bet, const float* eg, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  if (tid < 64) {   // level 1
+    const int o = 8 * (tid >> 3), j = tid & 7;
+    float x[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const float4* rp = reinterpret_cast<const float4*>(A + (o + m) * kLdA + o);
+      const float4 r0 = rp[0], r1 = rp[1];
+      const float a[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
       float acc = (m == j) ? 1.0f : 0.0f;
 #pragma unroll
-      for (int l = 0; l < m; ++l) acc = fmaf(A[(o + m) * kLdA + o + l], x[l], acc);
+      for (int l = 0; l < m; ++l) acc = fmaf(a[l], x[l], acc);
       x[m] = acc;
     }
 #pragma unroll
-    for (int m = 0; m < 16; ++m) T[(o + m) * kLdA + o + j] = x[m];
+    for (int m = 0; m < 8; ++m) {
+      T[(o + m) * kLdA + o + j] = x[m];
+      st_tp_one(smem, o + m, o + j, x[m], bet, eg);
+    }
   }
   __syncthreads();
-#pragma unroll 1
-  for (int d = 1; d < 4; ++d) {
-    const int nblk = 4 - d;
-    // X_i = sum_{k=i-d}^{i-1} A_{i,k} T_{k,i-d}, blocks i = d..3
-    for (int e = tid; e < nblk * 256; e += kPrefillThreads) {
-      const int i = d + (e >> 8), m = (e >> 4) & 15, n = e & 15, jb = i - d;
-      float acc = 0.f;
-      for (int kb = jb; kb < i; ++kb) {
+  {  // level 2: X_p = A_hl T_ll, then T_hl = T_hh X_p, (hi, lo) = (16p + 8, 16p)
+    const int pr = tid >> 6, m = (tid >> 3) & 7, n = tid & 7;
+    const int lo = 16 * pr, hi = lo + 8;
+    float x = 0.f;
 #pragma unroll
-        for (int l = 0; l < 16; ++l)
-          acc = fmaf(A[(16 * i + m) * kLdA + 16 * kb + l], T[(16 * kb + l) * kLdA + 16 * jb + n], acc);
-      }
-      X[e] = acc;
-    }
+    for (int l = 0; l < 8; ++l) x = fmaf(A[(hi + m) * kLdA + lo + l], T[(lo + l) * kLdA + lo + n], x);
+    X[tid] = x;
     __syncthreads();
-    // T_{i,i-d} = T_ii X_i
-    for (int e = tid; e < nblk * 256; e += kPrefillThreads) {
-      const int i = d + (e >> 8), m = (e >> 4) & 15, n = e & 15, jb = i - d;
-      const float* Xi = X + (e & ~255);
-      float acc = 0.f;
+    float y = 0.f;
 #pragma unroll
-      for (int l = 0; l < 16; ++l)
-        if (l <= m) acc = fmaf(T[(16 * i + m) * kLdA + 16 * i + l], Xi[l * 16 + n], acc);
-      T[(16 * i + m) * kLdA + 16 * jb + n] = acc;
-    }
-    __syncthreads();
+    for (int l = 0; l < 8; ++l) y = fmaf(T[(hi + m) * kLdA + hi + l], X[pr * 64 + l * 8 + n], y);
+    T[(hi + m) * kLdA + lo + n] = y;
+    st_tp_one(smem, hi + m, lo + n, y, bet, eg);
   }
+  __syncthreads();
+  constexpr int kLdB = 24;    // pitch of the 16x16 scratch tiles (conflict-free B fragments)
+  if (warp < 4) {  // level 3a: X_p = A_hl T_ll for (hi, lo) = (32p + 16, 32p), 16x16
+    const int pr = warp >> 1, nt = warp & 1, lo = 32 * pr, hi = lo + 16;
+    float d[4];
+    mma_tile_3xtf32<2>(d, A + hi * kLdA + lo, kLdA, T + lo * kLdA + lo + 8 * nt, kLdA, lane);
+    const int g = lane >> 2, t = lane & 3;
+    float* Xp = X + pr * 16 * kLdB + 8 * nt;
+    *reinterpret_cast<float2*>(Xp + g * kLdB + 2 * t) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(Xp + (g + 8) * kLdB + 2 * t) = make_float2(d[2], d[3]);
+  }
+  __syncthreads();
+  if (warp < 4) {  // level 3b: T_hl = T_hh X_p
+    const int pr = warp >> 1, nt = warp & 1, lo = 32 * pr, hi = lo + 16;
+    float d[4];
+    mma_tile_3xtf32<2>(d, T + hi * kLdA + hi, kLdA, X + pr * 16 * kLdB + 8 * nt, kLdB, lane);
+    const int g = lane >> 2, t = lane & 3;
+    const int col = lo + 8 * nt + 2 * t;
+    *reinterpret_cast<float2*>(T + (hi + g) * kLdA + col) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(T + (hi + g + 8) * kLdA + col) = make_float2(d[2], d[3]);
+    st_tp_pair(smem, hi + g, col, d[0], d[1], bet, eg);
+    st_tp_pair(smem, hi + g + 8, col, d[2], d[3], bet, eg);
+  }
+  __syncthreads();
+  constexpr int kLdC = 40;    // pitch of the 32x32 scratch tile
+  const int mt = warp >> 2, nt = warp & 3;
+  {  // level 4a: X = A[32:64, 0:32] T[0:32, 0:32]
+    float d[4];
+    mma_tile_3xtf32<4>(d, A + (32 + 16 * mt) * kLdA, kLdA, T + 8 * nt, kLdA, lane);
+    const int g = lane >> 2, t = lane & 3;
+    float* Xp = X + 16 * mt * kLdC + 8 * nt;
+    *reinterpret_cast<float2*>(Xp + g * kLdC + 2 * t) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(Xp + (g + 8) * kLdC + 2 * t) = make_float2(d[2], d[3]);
+  }
+  __syncthreads();
+  {  // level 4b: T[32:64, 0:32] = T[32:64, 32:64] X  (only the bf16 tiles need it)
+    float d[4];
+    mma_tile_3xtf32<4>(d, T + (32 + 16 * mt) * kLdA + 32, kLdA, X + 8 * nt, kLdC, lane);
+    const int g = lane >> 2, t = lane & 3;
+    const int row = 32 + 16 * mt + g, col = 8 * nt + 2 * t;
+    st_tp_pair(smem, row, col, d[0], d[1], bet, eg);
+    st_tp_pair(smem, row + 8, col, d[2], d[3], bet, eg);
+  }
+}
+
+// Gates of one chunk (one warp, two positions per lane).  gate_inputs loads
+// a and b (issued early, so their latency hides behind other work);
+// gate_finish forms log g, its inclusive prefix sum gamma, e^gamma and beta.
+// Positions past the sequence end get log g = 0 and beta = 0.
+struct GateIn {
+  float a[2], b[2];
+  bool valid[2];
+};
+
+__device__ __forceinline__ GateIn gate_inputs(const PrefillParams& p, long long cstart, int clen,
+                                              int head, int lane) {
+  GateIn g;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int pos = 2 * lane + e;
+    g.valid[e] = pos < clen;
+    if (g.valid[e]) {
+      const size_t t = static_cast<size_t>(cstart + pos) * p.h_v + head;
+      g.a[e] = __bfloat162float(p.a[t]);
+      g.b[e] = __bfloat162float(p.b[t]);
+    } else {
+      g.a[e] = g.b[e] = 0.f;
+    }
+  }
+  return g;
+}
+
+__device__ __forceinline__ void gate_finish(const GateIn& g, float A_neg, float dtb, int lane,
+                                            float* gam, float* bet, float* eg) {
+  float lg[2], bt[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    lg[e] = g.valid[e] ? A_neg * softplus20p(g.a[e] + dtb) : 0.f;
+    bt[e] = g.valid[e] ? 1.0f / (1.0f + expf(-g.b[e])) : 0.f;
+  }
+  float x = lg[0] + lg[1];
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  const float g0 = (x - (lg[0] + lg[1])) + lg[0], g1 = g0 + lg[1];
+  gam[2 * lane] = g0;
+  gam[2 * lane + 1] = g1;
+  eg[2 * lane] = expf(g0);
+  eg[2 * lane + 1] = expf(g1);
+  bet[2 * lane] = bt[0];
+  bet[2 * lane + 1] = bt[1];
 }
 
 __global__ void __launch_bounds__(kPrefillThreads, 1)
@@ -204,38 +374,79 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     return;
   }
 
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* bar_mma = bar_tma + 1;
+  uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + kOffBar);   // Q + K copy -> QKW
+  uint64_t* bar_k = bar_q + 1;                                      // K -> KB
+  uint64_t* bar_v = bar_q + 2;                                      // V -> VB
+  uint64_t* bar_mma = bar_q + 3;                                    // UMMA groups
+  uint64_t* bar_mma2 = bar_q + 4;                                   // second UMMA group of a step
   uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + kOffTmemPtr);
   float* AF = reinterpret_cast<float*>(smem + kOffAF);
   float* TF = reinterpret_cast<float*>(smem + kOffTF);
   float* XS = reinterpret_cast<float*>(smem + kOffXS);
-  float* gam = reinterpret_cast<float*>(smem + kOffGam);
-  float* bet = reinterpret_cast<float*>(smem + kOffBeta);
-  float* eg = reinterpret_cast<float*>(smem + kOffEG);
+  float* gate_base = reinterpret_cast<float*>(smem + kOffGate);
+
+  const float A_neg = -expf(p.A_log[head]);
+  const float dtb = p.dt_bias[head];
+  const int nchunks = static_cast<int>((len + kChunk - 1) / kChunk);
+
+  auto load_q = [&](long long cstart) {
+    mbar_arrive_expect_tx(bar_q, 4 * kTileBytes);
+    const int t0 = static_cast<int>(cstart);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+      tma_load_3d(smem + kOffQKW + kb * 16384, &tm_q, bar_q, kb * 64, hq, t0);
+      tma_load_3d(smem + kOffQKW + kb * 16384 + 8192, &tm_k, bar_q, kb * 64, hq, t0);
+    }
+  };
+  auto load_k = [&](long long cstart) {
+    mbar_arrive_expect_tx(bar_k, 2 * kTileBytes);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+      tma_load_3d(smem + kOffKB + kb * 8192, &tm_k, bar_k, kb * 64, hq, static_cast<int>(cstart));
+  };
+  auto load_v = [&](long long cstart) {
+    mbar_arrive_expect_tx(bar_v, 2 * kTileBytes);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+      tma_load_3d(smem + kOffVB + kb * 8192, &tm_v, bar_v, kb * 64, head, static_cast<int>(cstart));
+  };
 
   if (warp == 0) {
     tmem_alloc(tmem_ptr, kTmCols);
     tmem_relinquish();
   }
   if (tid == 32) {
-    mbar_init(bar_tma, 1);
-    mbar_init(bar_mma, 1);
+    for (int i = 0; i < 5; ++i) mbar_init(bar_q + i, 1);
     fence_mbarrier_init();
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  // Zero block Z of the stacked A operands.
-  reinterpret_cast<uint4*>(smem + kOffTPZT + 16384)[tid] = make_uint4(0, 0, 0, 0);
-  reinterpret_cast<uint4*>(smem + kOffTPZT + 16384)[tid + 256] = make_uint4(0, 0, 0, 0);
+  // Zero the whole T' | P | Z | T_b region (Z stays zero; the upper triangles of
+  // T' and T_b are never written again) and the fp32 T (its strictly-upper
+  // blocks stay zero).
+  for (int i = tid; i < 32768 / 16; i += kPrefillThreads)
+    reinterpret_cast<uint4*>(smem + kOffTPZT)[i] = make_uint4(0, 0, 0, 0);
+  for (int i = tid; i < 64 * kLdA / 4; i += kPrefillThreads)
+    reinterpret_cast<float4*>(TF)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  if (tid == 0) {   // chunk 0 tiles
+    load_q(s0);
+    load_k(s0);
+    load_v(s0);
+  }
+  if (warp == 1) {
+    const GateIn g0 = gate_inputs(p, s0, static_cast<int>(min(static_cast<long long>(kChunk), len)),
+                                  head, lane);
+    gate_finish(g0, A_neg, dtb, lane, gate_base, gate_base + 64, gate_base + 128);
+  }
 
   // Initial state: thread (k = row, half) holds S^T[k][64*half + j] = S[64*half + j][k].
   float sreg[64];
 #pragma unroll
   for (int j = 0; j < 64; ++j)
     sreg[j] = p.state ? p.state[sbase + static_cast<size_t>(64 * half + j) * kHeadDim + row] : 0.f;
-  st_row_bf16(smem + kOffSB + half * 16384, row, sreg, 1.0f);
+  st_row_bf16(smem + kOffSB + half * 16384, row, sreg);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -251,70 +462,54 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   const uint32_t a_vn = smem_u32(smem + kOffVN);
   const uint32_t a_vnd = smem_u32(smem + kOffVND);
 
-  const float A_neg = -expf(p.A_log[head]);
-  const float dtb = p.dt_bias[head];
-
-  uint32_t ph_tma = 0, ph_mma = 0;
-  unsigned int fail = 0;
-  const int nchunks = static_cast<int>((len + kChunk - 1) / kChunk);
+  uint32_t ph = 0;            // phase of the per-chunk barriers (each completes once per chunk)
+  uint32_t ph_mma = 0, ph_mma2 = 0;
+  GateIn next_gates;          // warp 1: the next chunk's a, b, loaded one chunk ahead
+  bool failed = false;        // this thread saw a wait run out
+  unsigned int fail_code = 0;
+  uint64_t* fail_bar = nullptr;
+  uint32_t fail_parity = 0;
+  auto wait = [&](uint64_t* bar, uint32_t parity, unsigned int code) {
+    if (!mbar_wait(bar, parity)) {
+      if (!failed) {
+        fail_bar = bar;
+        fail_parity = parity;
+      }
+      failed = true;
+      fail_code |= code;
+    }
+  };
+  auto mma_done = [&]() {
+    wait(bar_mma, ph_mma, kStatusMmaTimeout);
+    ph_mma ^= 1;
+    tc_fence_after();
+  };
+  auto mma2_done = [&]() {
+    wait(bar_mma2, ph_mma2, kStatusMmaTimeout);
+    ph_mma2 ^= 1;
+    tc_fence_after();
+  };
 
   for (int ci = 0; ci < nchunks; ++ci) {
     const long long cstart = s0 + static_cast<long long>(ci) * kChunk;
     const int clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - cstart));
+    const bool has_next = ci + 1 < nchunks;
+    const long long nstart = cstart + kChunk;
+    const float* gam = gate_base + (ci & 1) * 192;
+    const float* bet = gam + 64;
+    const float* eg = gam + 128;
 
-    // ---- 1. TMA: Q and K into the stacked operand, K and V tiles.
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar_tma, kTmaBytesPerChunk);
-      const int t0 = static_cast<int>(cstart);
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
-        tma_load_3d(smem + kOffQKW + kb * 16384, &tm_q, bar_tma, kb * 64, hq, t0);
-        tma_load_3d(smem + kOffQKW + kb * 16384 + 8192, &tm_k, bar_tma, kb * 64, hq, t0);
-        tma_load_3d(smem + kOffKB + kb * 8192, &tm_k, bar_tma, kb * 64, hq, t0);
-        tma_load_3d(smem + kOffVB + kb * 8192, &tm_v, bar_tma, kb * 64, head, t0);
-      }
-    }
-    // ---- gates: log g, its inclusive prefix sum, beta (warp 1).
-    if (warp == 1) {
-      float lg[2], bt[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int pos = 2 * lane + e;
-        if (pos < clen) {
-          const size_t t = static_cast<size_t>(cstart + pos) * p.h_v + head;
-          const float av = __bfloat162float(p.a[t]);
-          const float bv = __bfloat162float(p.b[t]);
-          lg[e] = A_neg * softplus20p(av + dtb);
-          bt[e] = 1.0f / (1.0f + expf(-bv));
-        } else {
-          lg[e] = 0.f;
-          bt[e] = 0.f;
-        }
-      }
-      float x = lg[0] + lg[1];
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, x, off);
-        if (lane >= off) x += y;
-      }
-      const float excl = x - (lg[0] + lg[1]);
-      const float g0 = excl + lg[0], g1 = g0 + lg[1];
-      gam[2 * lane] = g0;
-      gam[2 * lane + 1] = g1;
-      eg[2 * lane] = expf(g0);
-      eg[2 * lane + 1] = expf(g1);
-      bet[2 * lane] = bt[0];
-      bet[2 * lane + 1] = bt[1];
-    }
-    __syncthreads();
-    {
-      const bool ok = mbar_wait(bar_tma, ph_tma);
-      if (__syncthreads_or(!ok)) { fail = kStatusTmaTimeout; break; }
-      ph_tma ^= 1;
-    }
-    // Tail chunk: rows past the sequence end hold the next sequence's tokens
-    // (or TMA zero fill); clear them so that 0 * (non-finite input) cannot reach S.
+    // ---- 1. wait for this chunk's Q/K tiles (requested during the previous chunk).
+    if (warp == 1 && has_next)
+      next_gates = gate_inputs(p, nstart,
+                               static_cast<int>(min(static_cast<long long>(kChunk), s1 - nstart)),
+                               head, lane);
+    wait(bar_q, ph, kStatusTmaTimeout);
+    wait(bar_k, ph, kStatusTmaTimeout);
     if (clen < kChunk) {
+      // Tail chunk: rows past the sequence end hold the next sequence's tokens
+      // (or TMA zero fill); clear them so that 0 * (non-finite input) cannot reach S.
+      wait(bar_v, ph, kStatusTmaTimeout);
       const int nrow = kChunk - clen;
       for (int e = tid; e < 8 * nrow * 8; e += kPrefillThreads) {
         const int reg = e / (nrow * 8);            // 8 row-blocks of 64 rows x 128 B
@@ -340,34 +535,44 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
       umma_commit(bar_mma);
     }
-    {
-      const bool ok = mbar_wait(bar_mma, ph_mma);
-      if (__syncthreads_or(!ok)) { fail = kStatusMmaTimeout; break; }
-      ph_mma ^= 1;
-    }
-    tc_fence_after();
+    mma_done();
 
-    // ---- 3. P (rows 0-63) to bf16, A (rows 64-127) to fp32.
+    // ---- 3. P (rows 0-63) to bf16, A (rows 64-127) to fp32.  A tile whose 32
+    // columns all lie above the diagonal is zero and skips the exponentials.
     {
-      float r[32];
-      tmem_ld32(tmem + tm_lane + kTmQK + 32 * half, r);
-      tmem_wait_ld();
+      const int i = row & 63;
+      const bool upper = half == 1 && (quad & 1) == 0;   // rows 0-31 x cols 32-63
       if (row < 64) {
-        const int i = row;
-        const float gi = gam[i];
+        uint8_t* ptile = smem + kOffTPZT + 8192;
+        if (upper) {
+          zero_half_row(ptile, i, 4);
+        } else {
+          float r[32];
+          tmem_ld32(tmem + tm_lane + kTmQK + 32 * half, r);
+          tmem_wait_ld();
+          const float gi = gam[i];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * half + jj;
-          r[jj] = (j <= i && i < clen) ? r[jj] * expf(gi - gam[j]) : 0.f;
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = 32 * half + jj;
+            r[jj] = (j <= i && i < clen) ? r[jj] * __expf(gi - gam[j]) : 0.f;
+          }
+          st_half_row_bf16(ptile, i, 4 * half, r, 1.0f);
         }
-        st_half_row_bf16(smem + kOffTPZT + 8192, i, 4 * half, r, 1.0f);
-      } else {
-        const int i = row - 64;
+      } else if (!upper) {
+        float r[32];
+        tmem_ld32(tmem + tm_lane + kTmQK + 32 * half, r);
+        tmem_wait_ld();
         const float gi = gam[i], nb = -bet[i];
+        float* arow = AF + i * kLdA + 32 * half;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
+        for (int jj = 0; jj < 32; jj += 4) {
+          float4 o;
           const int j = 32 * half + jj;
-          AF[i * kLdA + j] = (j < i && i < clen) ? nb * r[jj] * expf(gi - gam[j]) : 0.f;
+          o.x = (j + 0 < i && i < clen) ? nb * r[jj + 0] * __expf(gi - gam[j + 0]) : 0.f;
+          o.y = (j + 1 < i && i < clen) ? nb * r[jj + 1] * __expf(gi - gam[j + 1]) : 0.f;
+          o.z = (j + 2 < i && i < clen) ? nb * r[jj + 2] * __expf(gi - gam[j + 2]) : 0.f;
+          o.w = (j + 3 < i && i < clen) ? nb * r[jj + 3] * __expf(gi - gam[j + 3]) : 0.f;
+          *reinterpret_cast<float4*>(arow + jj) = o;
         }
       }
     }
@@ -375,38 +580,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     __syncthreads();
 
     // ---- 4. T = (I - A)^{-1};  T' = T diag(beta e^gamma),  T_b = T diag(beta).
-    solve_unit_lower(AF, TF, XS, tid);
-    {
-      const int i = tid >> 2, j0 = (tid & 3) * 16;
-      float tp[16], tb[16];
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const int j = j0 + jj;
-        const float t = (j <= i) ? TF[i * kLdA + j] : 0.f;
-        tb[jj] = t * bet[j];
-        tp[jj] = tb[jj] * eg[j];
-      }
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint4 u, w;
-        u.x = pack_bf16x2(tp[8 * h2 + 0], tp[8 * h2 + 1]);
-        u.y = pack_bf16x2(tp[8 * h2 + 2], tp[8 * h2 + 3]);
-        u.z = pack_bf16x2(tp[8 * h2 + 4], tp[8 * h2 + 5]);
-        u.w = pack_bf16x2(tp[8 * h2 + 6], tp[8 * h2 + 7]);
-        w.x = pack_bf16x2(tb[8 * h2 + 0], tb[8 * h2 + 1]);
-        w.y = pack_bf16x2(tb[8 * h2 + 2], tb[8 * h2 + 3]);
-        w.z = pack_bf16x2(tb[8 * h2 + 4], tb[8 * h2 + 5]);
-        w.w = pack_bf16x2(tb[8 * h2 + 6], tb[8 * h2 + 7]);
-        const uint32_t off = sw128_off(i, (tid & 3) * 2 + h2);
-        *reinterpret_cast<uint4*>(smem + kOffTPZT + off) = u;           // T'
-        *reinterpret_cast<uint4*>(smem + kOffTPZT + 24576 + off) = w;   // T_b
-      }
-    }
+    solve_unit_lower(AF, TF, XS, smem, bet, eg, tid);
     fence_proxy_async_smem();
     __syncthreads();
 
     // ---- 5. D_W = [T' ; P] K,  D_UO = [Z ; T_b] V.
     if (tid == 0) {
+      if (clen == kChunk) wait(bar_v, ph, kStatusTmaTimeout);
       tc_fence_after();
       const uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
 #pragma unroll
@@ -414,30 +594,23 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         umma_bf16(tmem + kTmW, sdesc_sw128(a_tpzt + s * 32, 16, 1024),
                   sdesc_sw128(a_kb + s * 2048, 8192, 1024), idesc, s > 0 ? 1u : 0u);
       }
+      umma_commit(bar_mma);    // W first: its epilogue starts while U is computed
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         umma_bf16(tmem + kTmUO, sdesc_sw128(a_tpzt + 16384 + s * 32, 16, 1024),
                   sdesc_sw128(a_vb + s * 2048, 8192, 1024), idesc, s > 0 ? 1u : 0u);
       }
-      umma_commit(bar_mma);
+      umma_commit(bar_mma2);
     }
-    {
-      const bool ok = mbar_wait(bar_mma, ph_mma);
-      if (__syncthreads_or(!ok)) { fail = kStatusMmaTimeout; break; }
-      ph_mma ^= 1;
-    }
-    tc_fence_after();
 
     // ---- 6. -W into rows 64-127 of the stacked operand; Q <- e^gamma Q in rows 0-63.
     if (row < 64) {
+      mma_done();
+      float r[64];
+      tmem_ld64(tmem + tm_lane + kTmW + 64 * half, r);
       uint8_t* tile = smem + kOffQKW + half * 16384;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float r[32];
-        tmem_ld32(tmem + tm_lane + kTmW + 64 * half + 32 * hh, r);
-        tmem_wait_ld();
-        st_half_row_bf16(tile, 64 + row, 4 * hh, r, -1.0f);
-      }
+      st_half_row_bf16(tile, 64 + row, 0, r, -1.0f);
+      st_half_row_bf16(tile, 64 + row, 4, r + 32, -1.0f);
     } else {
       const int c = row - 64;
       const float e = eg[c];
@@ -455,6 +628,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
         *ptr = u;
       }
+      ph_mma ^= 1;   // this thread does not read D_W
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -462,7 +636,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 
     // ---- 7. D_UO += [e^g Q ; -W] S^T.
     if (tid == 0) {
-      tc_fence_after();
+      mma2_done();                                // U is in D_UO
+      if (has_next) load_v(nstart);               // VB is free once the U product completed
       const uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
@@ -471,27 +646,26 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
       umma_commit(bar_mma);
     }
-    {
-      const bool ok = mbar_wait(bar_mma, ph_mma);
-      if (__syncthreads_or(!ok)) { fail = kStatusMmaTimeout; break; }
-      ph_mma ^= 1;
-    }
-    tc_fence_after();
+    if (tid != 0) ph_mma2 ^= 1;   // the U group was consumed by thread 0 alone
+    mma_done();
+    if (tid == 0 && has_next) load_q(nstart);   // QKW is free once the S^T product completed
 
     const float gam_last = gam[clen - 1];
-    // ---- 8. v_new (rows 64-127) to bf16, plus its decayed copy.
+    // ---- 8. v_new (rows 64-127) to bf16 plus its decayed copy; meanwhile warp 1
+    // computes the next chunk's gates into the other gate buffer.
     if (row >= 64) {
       const int c = row - 64;
-      const float dec = (c < clen) ? expf(gam_last - gam[c]) : 0.f;
+      const float dec = (c < clen) ? __expf(gam_last - gam[c]) : 0.f;
       const float keep = (c < clen) ? 1.f : 0.f;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float r[32];
-        tmem_ld32(tmem + tm_lane + kTmUO + 64 * half + 32 * hh, r);
-        tmem_wait_ld();
-        st_half_row_bf16(smem + kOffVN + half * 8192, c, 4 * hh, r, keep);
-        st_half_row_bf16(smem + kOffVND + half * 8192, c, 4 * hh, r, dec);
-      }
+      float r[64];
+      tmem_ld64(tmem + tm_lane + kTmUO + 64 * half, r);
+      st_half_row_bf16(smem + kOffVN + half * 8192, c, 0, r, keep);
+      st_half_row_bf16(smem + kOffVN + half * 8192, c, 4, r + 32, keep);
+      st_half_row_bf16(smem + kOffVND + half * 8192, c, 0, r, dec);
+      st_half_row_bf16(smem + kOffVND + half * 8192, c, 4, r + 32, dec);
+    } else if (warp == 1 && has_next) {
+      float* ng = gate_base + ((ci + 1) & 1) * 192;
+      gate_finish(next_gates, A_neg, dtb, lane, ng, ng + 64, ng + 128);
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -504,70 +678,62 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, 1, 1);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        umma_bf16(tmem + kTmUO, sdesc_sw128(a_tpzt + 8192 + s * 32, 16, 1024),
-                  sdesc_sw128(a_vn + s * 2048, 8192, 1024), idesc_o, 1u);
-      }
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
         umma_bf16(tmem + kTmS4, sdesc_sw128(a_kb + s * 2048, 8192, 1024),
                   sdesc_sw128(a_vnd + s * 2048, 8192, 1024), idesc_s, s > 0 ? 1u : 0u);
       }
-      umma_commit(bar_mma);
+      umma_commit(bar_mma);    // the state increment first: it is on the chunk chain
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        umma_bf16(tmem + kTmUO, sdesc_sw128(a_tpzt + 8192 + s * 32, 16, 1024),
+                  sdesc_sw128(a_vn + s * 2048, 8192, 1024), idesc_o, 1u);
+      }
+      umma_commit(bar_mma2);
     }
-    {
-      const bool ok = mbar_wait(bar_mma, ph_mma);
-      if (__syncthreads_or(!ok)) { fail = kStatusMmaTimeout; break; }
-      ph_mma ^= 1;
-    }
-    tc_fence_after();
+    mma_done();
+    if (tid == 0 && has_next) load_k(nstart);   // KB is free once the state product completed
 
-    // ---- 10. Output rows (0-63) and the state update (all rows).
+    // ---- 10. State update (all rows) and output rows (0-63).
+    {
+      const float decay = __expf(gam_last);
+      float r[64];
+      tmem_ld64(tmem + tm_lane + kTmS4 + 64 * half, r);
+#pragma unroll
+      for (int jj = 0; jj < 64; ++jj) sreg[jj] = fmaf(decay, sreg[jj], r[jj]);
+      st_row_bf16(smem + kOffSB + half * 16384, row, sreg);
+    }
     if (row < 64) {
-      __nv_bfloat16* orow = p.out + (static_cast<size_t>(cstart + row) * p.h_v + head) * kHeadDim +
-                            64 * half;
+      mma2_done();
+      float r[64];
+      tmem_ld64(tmem + tm_lane + kTmUO + 64 * half, r);
+      if (row < clen) {
+        __nv_bfloat16* orow = p.out + (static_cast<size_t>(cstart + row) * p.h_v + head) *
+                                          kHeadDim + 64 * half;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float r[32];
-        tmem_ld32(tmem + tm_lane + kTmUO + 64 * half + 32 * hh, r);
-        tmem_wait_ld();
-        if (row < clen) {
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            uint4 u;
-            u.x = pack_bf16x2(p.scale * r[8 * cc + 0], p.scale * r[8 * cc + 1]);
-            u.y = pack_bf16x2(p.scale * r[8 * cc + 2], p.scale * r[8 * cc + 3]);
-            u.z = pack_bf16x2(p.scale * r[8 * cc + 4], p.scale * r[8 * cc + 5]);
-            u.w = pack_bf16x2(p.scale * r[8 * cc + 6], p.scale * r[8 * cc + 7]);
-            *reinterpret_cast<uint4*>(orow + 32 * hh + 8 * cc) = u;
-          }
+        for (int cc = 0; cc < 8; ++cc) {
+          uint4 u;
+          u.x = pack_bf16x2(p.scale * r[8 * cc + 0], p.scale * r[8 * cc + 1]);
+          u.y = pack_bf16x2(p.scale * r[8 * cc + 2], p.scale * r[8 * cc + 3]);
+          u.z = pack_bf16x2(p.scale * r[8 * cc + 4], p.scale * r[8 * cc + 5]);
+          u.w = pack_bf16x2(p.scale * r[8 * cc + 6], p.scale * r[8 * cc + 7]);
+          *reinterpret_cast<uint4*>(orow + 8 * cc) = u;
         }
       }
-    }
-    {
-      const float decay = expf(gam_last);
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float r[32];
-        tmem_ld32(tmem + tm_lane + kTmS4 + 64 * half + 32 * hh, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) sreg[32 * hh + jj] = fmaf(decay, sreg[32 * hh + jj], r[jj]);
-      }
-      st_row_bf16(smem + kOffSB + half * 16384, row, sreg, 1.0f);
+    } else {
+      ph_mma2 ^= 1;   // these rows hold no output
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    ph ^= 1;
+    if (__syncthreads_or(failed)) break;
   }
 
-  if (fail) {
-    // Give in-flight copies and UMMAs one more bounded wait before freeing TMEM.
-    if (tid == 0) {
-      atomicOr(p.status, fail);
-      (void)mbar_wait(fail == kStatusTmaTimeout ? bar_tma : bar_mma,
-                      fail == kStatusTmaTimeout ? ph_tma : ph_mma);
+  const bool any_fail = __syncthreads_or(failed);
+  if (any_fail) {
+    if (failed) {
+      atomicOr(p.status, fail_code);
+      // one more bounded wait for the copy or UMMA that did not arrive
+      if (lane == 0) (void)mbar_wait(fail_bar, fail_parity);
     }
-    __syncthreads();
   } else {
 #pragma unroll
     for (int j = 0; j < 64; ++j)
