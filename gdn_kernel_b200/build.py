@@ -59,7 +59,8 @@ def _sources(*names):
 
 def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> list:
     """Compile every shared library of the package; returns their paths."""
-    core_deps = _sources("gdn_b200.cu", "gdn_ptx.cuh", "decode_kernel.cuh", "prefill_kernel.cuh")
+    core_deps = _sources("gdn_b200.cu", "gdn_ptx.cuh", "decode_kernel.cuh", "prefill_kernel.cuh",
+                         "prefill_split.cuh")
     core_deps.append(os.path.join(INCLUDE, "gdn_b200.h"))
     if force or _stale(LIB, core_deps):
         cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, f"-I{INCLUDE}", "-o", LIB,
@@ -81,9 +82,11 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
     for target, src in ((TVM_DECODE, "tvm_ffi_decode.cc"), (TVM_PREFILL, "tvm_ffi_prefill.cc")):
         deps = _sources(src, "tvm_ffi_common.h") + [os.path.join(INCLUDE, "gdn_b200.h"), LIB]
         if force or _stale(target, deps):
+            cuda = os.path.dirname(os.path.dirname(_nvcc()))
             cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", f"-I{INCLUDE}", f"-I{tvm_inc}",
-                   f"-I{dl_inc}", "-o", target, os.path.join(CSRC, src), f"-L{PKG}", "-lgdn_b200",
-                   f"-L{tvm_lib}", "-ltvm_ffi", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tvm_lib}"]
+                   f"-I{dl_inc}", f"-I{cuda}/include", "-o", target, os.path.join(CSRC, src),
+                   f"-L{PKG}", "-lgdn_b200", f"-L{tvm_lib}", "-ltvm_ffi", f"-L{cuda}/lib64",
+                   "-lcudart", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tvm_lib}"]
             _run(cmd, verbose)
         built.append(target)
     return built

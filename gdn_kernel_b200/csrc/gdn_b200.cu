@@ -12,7 +12,7 @@
 
 #include "gdn_b200.h"
 #include "decode_kernel.cuh"
-#include "prefill_kernel.cuh"
+#include "prefill_split.cuh"
 
 namespace gdn {
 
@@ -57,6 +57,12 @@ int device_setup(unsigned int** status_out) {
     e = cudaFuncSetAttribute(gdn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPrefillSmem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill smem)");
+    e = cudaFuncSetAttribute(gdn_prefill_prep_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kP1Smem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prep smem)");
+    e = cudaFuncSetAttribute(gdn_prefill_chain_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kC2Smem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem)");
     s.status = static_cast<unsigned int*>(addr);
     s.done = true;
   }
@@ -165,14 +171,16 @@ extern "C" int gdn_b200_decode(const void* q, const void* k, const void* v, cons
   return GDN_B200_OK;
 }
 
-extern "C" int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* state,
-                                const float* A_log, const void* a, const float* dt_bias,
-                                const void* b, const void* cu_seqlens,
-                                int32_t cu_seqlens_is_int64, double scale, void* output,
-                                float* new_state, int64_t num_seqs, int64_t total_tokens,
-                                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
-                                void* stream) {
-  t_last_error.clear();
+namespace gdn {
+namespace {
+
+// Shared argument checks and parameter setup of both prefill entry points.
+int prefill_setup(const void* q, const void* k, const void* v, const float* state,
+                  const float* A_log, const void* a, const float* dt_bias, const void* b,
+                  const void* cu_seqlens, int32_t cu_seqlens_is_int64, double scale, void* output,
+                  float* new_state, int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                  int32_t num_v_heads, int32_t head_dim, PrefillParams* p, CUtensorMap* tq,
+                  CUtensorMap* tk, CUtensorMap* tv) {
   if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
   if (num_seqs < 0 || total_tokens < 0)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0");
@@ -202,31 +210,100 @@ extern "C" int gdn_b200_prefill(const void* q, const void* k, const void* v, con
   const void* qb = total_tokens > 0 ? q : new_state;
   const void* kb = total_tokens > 0 ? k : new_state;
   const void* vb = total_tokens > 0 ? v : new_state;
-  CUtensorMap tq, tk, tv;
-  if (int rc = make_token_map(&tq, qb, total_tokens > 0 ? num_qk_heads : 1, map_tokens)) return rc;
-  if (int rc = make_token_map(&tk, kb, total_tokens > 0 ? num_qk_heads : 1, map_tokens)) return rc;
-  if (int rc = make_token_map(&tv, vb, total_tokens > 0 ? num_v_heads : 1, map_tokens)) return rc;
+  if (int rc = make_token_map(tq, qb, total_tokens > 0 ? num_qk_heads : 1, map_tokens)) return rc;
+  if (int rc = make_token_map(tk, kb, total_tokens > 0 ? num_qk_heads : 1, map_tokens)) return rc;
+  if (int rc = make_token_map(tv, vb, total_tokens > 0 ? num_v_heads : 1, map_tokens)) return rc;
 
+  p->state = state;
+  p->A_log = A_log;
+  p->a = static_cast<const __nv_bfloat16*>(a);
+  p->dt_bias = dt_bias;
+  p->b = static_cast<const __nv_bfloat16*>(b);
+  p->cu_seqlens = cu_seqlens;
+  p->cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
+  p->total_tokens = total_tokens;
+  p->scale = resolve_scale(scale);
+  p->out = static_cast<__nv_bfloat16*>(output);
+  p->new_state = new_state;
+  p->h_qk = num_qk_heads;
+  p->h_v = num_v_heads;
+  p->status = status;
+  return GDN_B200_OK;
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* state,
+                                const float* A_log, const void* a, const float* dt_bias,
+                                const void* b, const void* cu_seqlens,
+                                int32_t cu_seqlens_is_int64, double scale, void* output,
+                                float* new_state, int64_t num_seqs, int64_t total_tokens,
+                                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                                void* stream) {
+  t_last_error.clear();
   PrefillParams p;
-  p.state = state;
-  p.A_log = A_log;
-  p.a = static_cast<const __nv_bfloat16*>(a);
-  p.dt_bias = dt_bias;
-  p.b = static_cast<const __nv_bfloat16*>(b);
-  p.cu_seqlens = cu_seqlens;
-  p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
-  p.total_tokens = total_tokens;
-  p.scale = resolve_scale(scale);
-  p.out = static_cast<__nv_bfloat16*>(output);
-  p.new_state = new_state;
-  p.h_qk = num_qk_heads;
-  p.h_v = num_v_heads;
-  p.status = status;
+  CUtensorMap tq, tk, tv;
+  if (int rc = prefill_setup(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64,
+                             scale, output, new_state, num_seqs, total_tokens, num_qk_heads,
+                             num_v_heads, head_dim, &p, &tq, &tk, &tv))
+    return rc;
+  if (num_seqs == 0) return GDN_B200_OK;
   const dim3 grid(static_cast<unsigned>(num_v_heads), static_cast<unsigned>(num_seqs));
   gdn_prefill_kernel<<<grid, kPrefillThreads, kPrefillSmem, static_cast<cudaStream_t>(stream)>>>(
       tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return GDN_B200_OK;
+}
+
+extern "C" uint64_t gdn_b200_prefill_workspace_size(int64_t num_seqs, int64_t total_tokens,
+                                                    int32_t num_v_heads) {
+  if (num_seqs <= 0 || total_tokens < 0 || num_v_heads <= 0) return 0;
+  return split_layout(num_seqs, total_tokens, num_v_heads).total;
+}
+
+extern "C" int gdn_b200_prefill_ws(const void* q, const void* k, const void* v,
+                                   const float* state, const float* A_log, const void* a,
+                                   const float* dt_bias, const void* b, const void* cu_seqlens,
+                                   int32_t cu_seqlens_is_int64, double scale, void* output,
+                                   float* new_state, int64_t num_seqs, int64_t total_tokens,
+                                   int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                                   void* workspace, uint64_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  PrefillParams p;
+  CUtensorMap tq, tk, tv;
+  if (int rc = prefill_setup(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64,
+                             scale, output, new_state, num_seqs, total_tokens, num_qk_heads,
+                             num_v_heads, head_dim, &p, &tq, &tk, &tv))
+    return rc;
+  if (num_seqs == 0) return GDN_B200_OK;
+  const SplitLayout L = split_layout(num_seqs, total_tokens, num_v_heads);
+  if (!workspace || workspace_bytes < L.total || !aligned(workspace, 256))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "workspace is null, not 256-byte aligned or smaller than "
+                "gdn_b200_prefill_workspace_size()");
+  if (L.max_chunks > 0x7fffffffLL)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "too many chunks");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  SplitParams sp;
+  sp.base = p;
+  sp.header = reinterpret_cast<int*>(ws + L.off_header);
+  sp.seq_off = reinterpret_cast<int*>(ws + L.off_seq);
+  sp.table = reinterpret_cast<ChunkInfo*>(ws + L.off_table);
+  sp.records = ws + L.off_rec;
+  sp.num_seqs = static_cast<int>(num_seqs);
+  sp.max_chunks = static_cast<int>(L.max_chunks);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  gdn_chunk_table_kernel<<<1, kTableThreads, 0, st>>>(sp);
+  if (L.max_chunks > 0) {
+    const dim3 g1(static_cast<unsigned>(L.max_chunks), static_cast<unsigned>(num_v_heads));
+    gdn_prefill_prep_kernel<<<g1, kPrefillThreads, kP1Smem, st>>>(tq, tk, sp);
+  }
+  const dim3 g2(static_cast<unsigned>(2 * num_v_heads), static_cast<unsigned>(num_seqs));
+  gdn_prefill_chain_kernel<<<g2, kPrefillThreads, kC2Smem, st>>>(tk, tv, sp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill (two-stage) launch");
   return GDN_B200_OK;
 }
 

@@ -25,8 +25,8 @@
 //   D_S4 [128x128] = K^T (v_new e^{gamma_last-gamma})   (S^T increment)
 // The fp32 state lives in registers of the 256 threads (thread = TMEM lane k,
 // column half), its bf16 copy is the MN-major B operand of the S^T products.
-// The 64x64 triangular inverse runs in fp32 on CUDA cores (blocked: 16x16
-// diagonal inverses, 16-level merges, one 32-level merge).
+// The 64x64 triangular inverse: two 32x32 diagonal blocks by forward
+// substitution on CUDA cores, one 32-level merge in 3xTF32 (fp32 accuracy).
 //
 // Pipelining: the next chunk's tiles are requested as soon as the buffer they
 // land in has been consumed (V after the U product, Q and K after the S^T
@@ -158,7 +158,9 @@ template <int KSTEPS>
 __device__ __forceinline__ void mma_tile_3xtf32(float (&d)[4], const float* L, int ldl,
                                                 const float* R, int ldr, int lane) {
   const int g = lane >> 2, t = lane & 3;
-  d[0] = d[1] = d[2] = d[3] = 0.f;
+  // Every (k-step, split term) product gets its own accumulator, so the 3*KSTEPS
+  // mma.sync issue back to back instead of forming one dependent chain.
+  float acc[3 * KSTEPS][4];
 #pragma unroll
   for (int ks = 0; ks < KSTEPS; ++ks) {
     const float av[4] = {L[g * ldl + 8 * ks + t], L[(g + 8) * ldl + 8 * ks + t],
@@ -175,104 +177,78 @@ __device__ __forceinline__ void mma_tile_3xtf32(float (&d)[4], const float* L, i
       bh[e] = to_tf32(bv[e]);
       bl[e] = to_tf32(bv[e] - __uint_as_float(bh[e]));
     }
-    mma_tf32(d, al, bh);
-    mma_tf32(d, ah, bl);
-    mma_tf32(d, ah, bh);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[3 * ks][e] = acc[3 * ks + 1][e] = acc[3 * ks + 2][e] = 0.f;
+    mma_tf32(acc[3 * ks], al, bh);
+    mma_tf32(acc[3 * ks + 1], ah, bl);
+    mma_tf32(acc[3 * ks + 2], ah, bh);
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 3 * KSTEPS; ++q) sum += acc[q][e];
+    d[e] = sum;
   }
 }
 
 // T'[i][j] = T[i][j] beta_j e^{gamma_j} and T_b[i][j] = T[i][j] beta_j, as bf16
 // into the K-major swizzled tiles T' (TPZT + 0) and T_b (TPZT + 24 KiB).
-__device__ __forceinline__ void st_tp_one(uint8_t* smem, int i, int j, float t, const float* bet,
+__device__ __forceinline__ void st_tp_one(uint8_t* tpzt, int i, int j, float t, const float* bet,
                                           const float* eg) {
   const uint32_t off = sw128_off(i, j >> 3) + (j & 7) * 2;
   const float tb = t * bet[j];
-  *reinterpret_cast<__nv_bfloat16*>(smem + kOffTPZT + 24576 + off) = __float2bfloat16(tb);
-  *reinterpret_cast<__nv_bfloat16*>(smem + kOffTPZT + off) = __float2bfloat16(tb * eg[j]);
+  *reinterpret_cast<__nv_bfloat16*>(tpzt + 24576 + off) = __float2bfloat16(tb);
+  *reinterpret_cast<__nv_bfloat16*>(tpzt + off) = __float2bfloat16(tb * eg[j]);
 }
 
-__device__ __forceinline__ void st_tp_pair(uint8_t* smem, int i, int j, float t0, float t1,
+__device__ __forceinline__ void st_tp_pair(uint8_t* tpzt, int i, int j, float t0, float t1,
                                            const float* bet, const float* eg) {
   const uint32_t off = sw128_off(i, j >> 3) + (j & 7) * 2;   // j even: 4-byte aligned pair
   const float b0 = t0 * bet[j], b1 = t1 * bet[j + 1];
-  *reinterpret_cast<uint32_t*>(smem + kOffTPZT + 24576 + off) = pack_bf16x2(b0, b1);
-  *reinterpret_cast<uint32_t*>(smem + kOffTPZT + off) = pack_bf16x2(b0 * eg[j], b1 * eg[j + 1]);
+  *reinterpret_cast<uint32_t*>(tpzt + 24576 + off) = pack_bf16x2(b0, b1);
+  *reinterpret_cast<uint32_t*>(tpzt + off) = pack_bf16x2(b0 * eg[j], b1 * eg[j + 1]);
 }
 
-// T = (I - A)^{-1} for the strictly lower 64x64 fp32 A (row pitch kLdA), by
-// block doubling; every level is one or two barrier-separated steps:
-//   1. T_bb = (I - A_bb)^{-1} for the eight 8x8 diagonal blocks (forward
-//      substitution, one column per thread, CUDA cores);
-//   2. 8 -> 16:  T_hl = T_hh (A_hl T_ll) for the four 8x8 sub-diagonal blocks;
-//   3. 16 -> 32: the same for the two 16x16 sub-diagonal blocks (3xTF32 mma);
-//   4. 32 -> 64: the same for the 32x32 lower-left block (3xTF32 mma).
-// Results go to T (fp32, read by the next level) and straight into the bf16
-// T' / T_b operand tiles.  T's strictly-upper 8x8 blocks and the upper parts of
-// the T' / T_b tiles are zeroed once per CTA and never written.
-__device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float* X, uint8_t* smem,
+// T = (I - A)^{-1} for the strictly lower 64x64 fp32 A (row pitch kLdA):
+//   1. the two 32x32 diagonal blocks T_bb = (I - A_bb)^{-1}: warp b, lane j
+//      solves column j of block b by forward substitution with the column in
+//      registers (no barrier inside; the other warps wait at one barrier);
+//   2. T_10 = T_11 (A_10 T_00): two 32x32 products on the tensor cores in
+//      3xTF32 (fp32-level accuracy), one barrier apart.
+// Results go to T (fp32, read by step 2) and straight into the bf16 T' / T_b
+// operand tiles.  The upper-right 32x32 blocks of the T' / T_b tiles are never
+// written and must hold zeros; T's upper-right block is never read.
+__device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float* X, uint8_t* tpzt,
                                                  const float* bet, const float* eg, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
-  if (tid < 64) {   // level 1
-    const int o = 8 * (tid >> 3), j = tid & 7;
-    float x[8];
+  if (warp < 2) {   // step 1
+    const int o = 32 * warp, j = lane;
+    float x[32];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const float4* rp = reinterpret_cast<const float4*>(A + (o + m) * kLdA + o);
-      const float4 r0 = rp[0], r1 = rp[1];
-      const float a[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    for (int m = 0; m < 32; ++m) {
       float acc = (m == j) ? 1.0f : 0.0f;
+      const float4* rp = reinterpret_cast<const float4*>(A + (o + m) * kLdA + o);
 #pragma unroll
-      for (int l = 0; l < m; ++l) acc = fmaf(a[l], x[l], acc);
+      for (int q = 0; q < (m + 3) / 4; ++q) {
+        const float4 a4 = rp[q];
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (4 * q + e < m) acc = fmaf(av[e], x[4 * q + e], acc);
+      }
       x[m] = acc;
     }
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
+    for (int m = 0; m < 32; ++m) {
       T[(o + m) * kLdA + o + j] = x[m];
-      st_tp_one(smem, o + m, o + j, x[m], bet, eg);
+      st_tp_one(tpzt, o + m, o + j, x[m], bet, eg);
     }
   }
   __syncthreads();
-  {  // level 2: X_p = A_hl T_ll, then T_hl = T_hh X_p, (hi, lo) = (16p + 8, 16p)
-    const int pr = tid >> 6, m = (tid >> 3) & 7, n = tid & 7;
-    const int lo = 16 * pr, hi = lo + 8;
-    float x = 0.f;
-#pragma unroll
-    for (int l = 0; l < 8; ++l) x = fmaf(A[(hi + m) * kLdA + lo + l], T[(lo + l) * kLdA + lo + n], x);
-    X[tid] = x;
-    __syncthreads();
-    float y = 0.f;
-#pragma unroll
-    for (int l = 0; l < 8; ++l) y = fmaf(T[(hi + m) * kLdA + hi + l], X[pr * 64 + l * 8 + n], y);
-    T[(hi + m) * kLdA + lo + n] = y;
-    st_tp_one(smem, hi + m, lo + n, y, bet, eg);
-  }
-  __syncthreads();
-  constexpr int kLdB = 24;    // pitch of the 16x16 scratch tiles (conflict-free B fragments)
-  if (warp < 4) {  // level 3a: X_p = A_hl T_ll for (hi, lo) = (32p + 16, 32p), 16x16
-    const int pr = warp >> 1, nt = warp & 1, lo = 32 * pr, hi = lo + 16;
-    float d[4];
-    mma_tile_3xtf32<2>(d, A + hi * kLdA + lo, kLdA, T + lo * kLdA + lo + 8 * nt, kLdA, lane);
-    const int g = lane >> 2, t = lane & 3;
-    float* Xp = X + pr * 16 * kLdB + 8 * nt;
-    *reinterpret_cast<float2*>(Xp + g * kLdB + 2 * t) = make_float2(d[0], d[1]);
-    *reinterpret_cast<float2*>(Xp + (g + 8) * kLdB + 2 * t) = make_float2(d[2], d[3]);
-  }
-  __syncthreads();
-  if (warp < 4) {  // level 3b: T_hl = T_hh X_p
-    const int pr = warp >> 1, nt = warp & 1, lo = 32 * pr, hi = lo + 16;
-    float d[4];
-    mma_tile_3xtf32<2>(d, T + hi * kLdA + hi, kLdA, X + pr * 16 * kLdB + 8 * nt, kLdB, lane);
-    const int g = lane >> 2, t = lane & 3;
-    const int col = lo + 8 * nt + 2 * t;
-    *reinterpret_cast<float2*>(T + (hi + g) * kLdA + col) = make_float2(d[0], d[1]);
-    *reinterpret_cast<float2*>(T + (hi + g + 8) * kLdA + col) = make_float2(d[2], d[3]);
-    st_tp_pair(smem, hi + g, col, d[0], d[1], bet, eg);
-    st_tp_pair(smem, hi + g + 8, col, d[2], d[3], bet, eg);
-  }
-  __syncthreads();
-  constexpr int kLdC = 40;    // pitch of the 32x32 scratch tile
+  constexpr int kLdC = 40;    // pitch of the 32x32 scratch tile (conflict-free B fragments)
   const int mt = warp >> 2, nt = warp & 3;
-  {  // level 4a: X = A[32:64, 0:32] T[0:32, 0:32]
+  {  // step 2a: X = A[32:64, 0:32] T[0:32, 0:32]
     float d[4];
     mma_tile_3xtf32<4>(d, A + (32 + 16 * mt) * kLdA, kLdA, T + 8 * nt, kLdA, lane);
     const int g = lane >> 2, t = lane & 3;
@@ -281,13 +257,75 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
     *reinterpret_cast<float2*>(Xp + (g + 8) * kLdC + 2 * t) = make_float2(d[2], d[3]);
   }
   __syncthreads();
-  {  // level 4b: T[32:64, 0:32] = T[32:64, 32:64] X  (only the bf16 tiles need it)
+  {  // step 2b: T[32:64, 0:32] = T[32:64, 32:64] X  (only the bf16 tiles need it)
     float d[4];
     mma_tile_3xtf32<4>(d, T + (32 + 16 * mt) * kLdA + 32, kLdA, X + 8 * nt, kLdC, lane);
     const int g = lane >> 2, t = lane & 3;
     const int row = 32 + 16 * mt + g, col = 8 * nt + 2 * t;
-    st_tp_pair(smem, row, col, d[0], d[1], bet, eg);
-    st_tp_pair(smem, row + 8, col, d[2], d[3], bet, eg);
+    st_tp_pair(tpzt, row, col, d[0], d[1], bet, eg);
+    st_tp_pair(tpzt, row + 8, col, d[2], d[3], bet, eg);
+  }
+}
+
+// P (rows 0-63 of D_QK) to the bf16 P tile and A (rows 64-127) to fp32, for
+// the TMEM lane `row` of this thread and the 32 columns of its `half`:
+//   P_ij = (QK^T)_ij e^{gamma_i - gamma_j}          (j <= i < clen, else 0)
+//   A_ij = -beta_i (KK^T)_ij e^{gamma_i - gamma_j}  (j < i < clen, else 0)
+// A 32-column tile that lies wholly above the diagonal skips the exponentials.
+__device__ __forceinline__ void pa_epilogue(uint32_t tm_qk, int row, int half, int quad, int clen,
+                                            const float* gam, const float* bet, uint8_t* ptile,
+                                            float* AF) {
+  const int i = row & 63;
+  const bool upper = half == 1 && (quad & 1) == 0;   // rows 0-31 x cols 32-63
+  if (row < 64) {
+    if (upper) {
+      zero_half_row(ptile, i, 4);
+    } else {
+      float r[32];
+      tmem_ld32(tm_qk + 32 * half, r);
+      tmem_wait_ld();
+      const float gi = gam[i];
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = 32 * half + jj;
+        r[jj] = (j <= i && i < clen) ? r[jj] * __expf(gi - gam[j]) : 0.f;
+      }
+      st_half_row_bf16(ptile, i, 4 * half, r, 1.0f);
+    }
+  } else if (!upper) {
+    float r[32];
+    tmem_ld32(tm_qk + 32 * half, r);
+    tmem_wait_ld();
+    const float gi = gam[i], nb = -bet[i];
+    float* arow = AF + i * kLdA + 32 * half;
+#pragma unroll
+    for (int jj = 0; jj < 32; jj += 4) {
+      float4 o;
+      const int j = 32 * half + jj;
+      o.x = (j + 0 < i && i < clen) ? nb * r[jj + 0] * __expf(gi - gam[j + 0]) : 0.f;
+      o.y = (j + 1 < i && i < clen) ? nb * r[jj + 1] * __expf(gi - gam[j + 1]) : 0.f;
+      o.z = (j + 2 < i && i < clen) ? nb * r[jj + 2] * __expf(gi - gam[j + 2]) : 0.f;
+      o.w = (j + 3 < i && i < clen) ? nb * r[jj + 3] * __expf(gi - gam[j + 3]) : 0.f;
+      *reinterpret_cast<float4*>(arow + jj) = o;
+    }
+  }
+}
+
+// Q <- e^gamma Q in place on one 128-byte row of one K-column of a stacked
+// K-major tile.
+__device__ __forceinline__ void scale_q_row(uint8_t* tile, int c, float e) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    uint4* ptr = reinterpret_cast<uint4*>(tile + sw128_off(c, cc));
+    uint4 u = *ptr;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int q2 = 0; q2 < 4; ++q2) {
+      __nv_bfloat162 h2 = *reinterpret_cast<__nv_bfloat162*>(&w[q2]);
+      float2 f = __bfloat1622float2(h2);
+      w[q2] = pack_bf16x2(f.x * e, f.y * e);
+    }
+    *ptr = u;
   }
 }
 
@@ -422,13 +460,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  // Zero the whole T' | P | Z | T_b region (Z stays zero; the upper triangles of
-  // T' and T_b are never written again) and the fp32 T (its strictly-upper
-  // blocks stay zero).
+  // Zero the whole T' | P | Z | T_b region: Z stays zero, and the upper-right
+  // blocks of T' and T_b are never written by the solve.
   for (int i = tid; i < 32768 / 16; i += kPrefillThreads)
     reinterpret_cast<uint4*>(smem + kOffTPZT)[i] = make_uint4(0, 0, 0, 0);
-  for (int i = tid; i < 64 * kLdA / 4; i += kPrefillThreads)
-    reinterpret_cast<float4*>(TF)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
   if (tid == 0) {   // chunk 0 tiles
     load_q(s0);
@@ -537,50 +572,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     }
     mma_done();
 
-    // ---- 3. P (rows 0-63) to bf16, A (rows 64-127) to fp32.  A tile whose 32
-    // columns all lie above the diagonal is zero and skips the exponentials.
-    {
-      const int i = row & 63;
-      const bool upper = half == 1 && (quad & 1) == 0;   // rows 0-31 x cols 32-63
-      if (row < 64) {
-        uint8_t* ptile = smem + kOffTPZT + 8192;
-        if (upper) {
-          zero_half_row(ptile, i, 4);
-        } else {
-          float r[32];
-          tmem_ld32(tmem + tm_lane + kTmQK + 32 * half, r);
-          tmem_wait_ld();
-          const float gi = gam[i];
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int j = 32 * half + jj;
-            r[jj] = (j <= i && i < clen) ? r[jj] * __expf(gi - gam[j]) : 0.f;
-          }
-          st_half_row_bf16(ptile, i, 4 * half, r, 1.0f);
-        }
-      } else if (!upper) {
-        float r[32];
-        tmem_ld32(tmem + tm_lane + kTmQK + 32 * half, r);
-        tmem_wait_ld();
-        const float gi = gam[i], nb = -bet[i];
-        float* arow = AF + i * kLdA + 32 * half;
-#pragma unroll
-        for (int jj = 0; jj < 32; jj += 4) {
-          float4 o;
-          const int j = 32 * half + jj;
-          o.x = (j + 0 < i && i < clen) ? nb * r[jj + 0] * __expf(gi - gam[j + 0]) : 0.f;
-          o.y = (j + 1 < i && i < clen) ? nb * r[jj + 1] * __expf(gi - gam[j + 1]) : 0.f;
-          o.z = (j + 2 < i && i < clen) ? nb * r[jj + 2] * __expf(gi - gam[j + 2]) : 0.f;
-          o.w = (j + 3 < i && i < clen) ? nb * r[jj + 3] * __expf(gi - gam[j + 3]) : 0.f;
-          *reinterpret_cast<float4*>(arow + jj) = o;
-        }
-      }
-    }
+    // ---- 3. P (rows 0-63) to bf16, A (rows 64-127) to fp32.
+    pa_epilogue(tmem + tm_lane + kTmQK, row, half, quad, clen, gam, bet, smem + kOffTPZT + 8192, AF);
     tc_fence_before();
     __syncthreads();
 
     // ---- 4. T = (I - A)^{-1};  T' = T diag(beta e^gamma),  T_b = T diag(beta).
-    solve_unit_lower(AF, TF, XS, smem, bet, eg, tid);
+    solve_unit_lower(AF, TF, XS, smem + kOffTPZT, bet, eg, tid);
     fence_proxy_async_smem();
     __syncthreads();
 
@@ -613,21 +611,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       st_half_row_bf16(tile, 64 + row, 4, r + 32, -1.0f);
     } else {
       const int c = row - 64;
-      const float e = eg[c];
-      uint8_t* tile = smem + kOffQKW + half * 16384;
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint4* ptr = reinterpret_cast<uint4*>(tile + sw128_off(c, cc));
-        uint4 u = *ptr;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-        for (int q2 = 0; q2 < 4; ++q2) {
-          __nv_bfloat162 h2 = *reinterpret_cast<__nv_bfloat162*>(&w[q2]);
-          float2 f = __bfloat1622float2(h2);
-          w[q2] = pack_bf16x2(f.x * e, f.y * e);
-        }
-        *ptr = u;
-      }
+      scale_q_row(smem + kOffQKW + half * 16384, c, eg[c]);
       ph_mma ^= 1;   // this thread does not read D_W
     }
     fence_proxy_async_smem();

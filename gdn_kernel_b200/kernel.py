@@ -87,14 +87,28 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state) -
         float(scale or 0.0), _ptr(output), _ptr(new_state), B, h_qk, h_v, D, _stream(dev)))
 
 
+PREFILL_PATHS = ("split", "fused")
+
+
+def prefill_workspace_bytes(num_seqs: int, total_tokens: int, num_v_heads: int) -> int:
+    """Device workspace of the two-stage prefill for this problem size."""
+    return int(_lib.load().gdn_b200_prefill_workspace_size(num_seqs, total_tokens, num_v_heads))
+
+
 def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
-                new_state) -> None:
+                new_state, *, path: str = "split", workspace=None) -> None:
     """Chunked prefill; same arguments as the reference prefill ``kernel``.
 
     q, k: [T, H_qk, 128] bf16 (packed tokens); v: [T, H_v, 128] bf16;
     state: [N, H_v, 128, 128] fp32 or None; a, b: [T, H_v] bf16;
     cu_seqlens: [N + 1] int32 or int64 on the same device;
     output: [T, H_v, 128] bf16; new_state: [N, H_v, 128, 128] fp32 (may be state).
+
+    ``path="split"`` (default) runs the two-stage kernels (parallel per-chunk
+    preparation, then the sequential state recurrence) with a device workspace
+    (``workspace``: a uint8 CUDA tensor of at least ``prefill_workspace_bytes``
+    bytes, allocated here when omitted); ``path="fused"`` runs the single
+    kernel that needs no workspace.  Both give the same results.
     """
     dev = _cuda_device(q)
     _require(q.dim() == 3 and v.dim() == 3, "q and v must be packed [T, H, D]")
@@ -116,11 +130,23 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
     _check(new_state, "new_state", torch.float32, (N, h_v, D, D), dev)
     if state is not None:
         _check(state, "state", torch.float32, (N, h_v, D, D), dev)
+    _require(path in PREFILL_PATHS, f"path must be one of {PREFILL_PATHS}")
     lib = _lib.load()
-    _lib.check(lib.gdn_b200_prefill(
-        _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
-        _ptr(cu_seqlens), 1 if cu_seqlens.dtype == torch.int64 else 0, float(scale or 0.0),
-        _ptr(output), _ptr(new_state), N, T, h_qk, h_v, D, _stream(dev)))
+    args = (_ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
+            _ptr(cu_seqlens), 1 if cu_seqlens.dtype == torch.int64 else 0, float(scale or 0.0),
+            _ptr(output), _ptr(new_state), N, T, h_qk, h_v, D)
+    if path == "fused" or N == 0:
+        _lib.check(lib.gdn_b200_prefill(*args, _stream(dev)))
+        return
+    need = prefill_workspace_bytes(N, T, h_v)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    _require(isinstance(workspace, torch.Tensor) and workspace.device == dev
+             and workspace.numel() * workspace.element_size() >= need,
+             f"workspace must be a tensor on {dev} of at least {need} bytes")
+    _lib.check(lib.gdn_b200_prefill_ws(*args, _ptr(workspace),
+                                       workspace.numel() * workspace.element_size(),
+                                       _stream(dev)))
 
 
 def decode(q, k, v, state, A_log, a, dt_bias, b, scale: float = 0.0, *, in_place: bool = False):
@@ -139,7 +165,7 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale: float = 0.0, *, in_place
 
 
 def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale: float = 0.0, *,
-            in_place: bool = False):
+            in_place: bool = False, path: str = "split"):
     """Allocating prefill: returns ``(output, new_state)``."""
     T, _, D = q.shape
     h_v = v.shape[1]
@@ -150,7 +176,8 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale: float = 0.0
         new_state = state
     else:
         new_state = torch.empty((N, h_v, D, D), dtype=torch.float32, device=q.device)
-    gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+    gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                path=path)
     return output, new_state
 
 

@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import dataclasses
 import heapq
+import io
 import math
 import multiprocessing as mp
 import os
@@ -175,7 +176,12 @@ def _worker_main(fn, rank, world, port, backend, result_q, pg_timeout_s):
         dist.init_process_group(backend, rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=pg_timeout_s))
         value = fn(rank, world)
-        result_q.put(WorkerResult(rank, True, value))
+        # Serialise by value: tensors put on a multiprocessing queue would
+        # otherwise be shared through a file descriptor that this process's
+        # resource sharer serves, which is gone once the process exits.
+        buf = io.BytesIO()
+        torch.save(value, buf)
+        result_q.put(WorkerResult(rank, True, buf.getvalue()))
     except BaseException:  # noqa: BLE001 - reported to the parent, never swallowed
         result_q.put(WorkerResult(rank, False, error=traceback.format_exc()))
     finally:
@@ -217,6 +223,8 @@ def launch_workers(fn: Callable[[int, int], object], world: int, port: Optional[
     while len(results) < world and time.monotonic() < deadline:
         try:
             res = result_q.get(timeout=0.2)
+            if res.ok:
+                res.value = torch.load(io.BytesIO(res.value), weights_only=False)
             results[res.rank] = res
         except queue_mod.Empty:
             if all(not p.is_alive() for p in procs) and result_q.empty():

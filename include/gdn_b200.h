@@ -69,6 +69,32 @@ int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* s
                      int32_t num_v_heads, int32_t head_dim, void* stream);
 
 /*
+ * Bytes of device workspace gdn_b200_prefill_ws needs for this problem size
+ * (0 when num_seqs <= 0).  The two-stage prefill keeps one 49 KiB record per
+ * (64-token chunk, v-head) plus small chunk tables.  No counterpart in the
+ * reference, whose single kernel needs no workspace.
+ */
+uint64_t gdn_b200_prefill_workspace_size(int64_t num_seqs, int64_t total_tokens,
+                                         int32_t num_v_heads);
+
+/*
+ * Same contract and results as gdn_b200_prefill (replaces the same reference
+ * entry point, solution/cuda/kernel_prefill.cu:300-339), computed in two stages:
+ * the S-independent work of every (chunk, v-head) in parallel across the GPU,
+ * then the sequential state recurrence per (sequence, v-head, 64-column V
+ * slice).  `workspace` is caller-owned device memory of at least
+ * gdn_b200_prefill_workspace_size() bytes, 256-byte aligned; its contents are
+ * scratch and must not be shared by calls that overlap on the GPU.
+ */
+int gdn_b200_prefill_ws(const void* q, const void* k, const void* v, const float* state,
+                        const float* A_log, const void* a, const float* dt_bias, const void* b,
+                        const void* cu_seqlens, int32_t cu_seqlens_is_int64, double scale,
+                        void* output, float* new_state,
+                        int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                        int32_t num_v_heads, int32_t head_dim,
+                        void* workspace, uint64_t workspace_bytes, void* stream);
+
+/*
  * Reads (and with clear != 0 resets) the status word that the kernels of
  * this library set on `device` when a bounded device-side wait runs out or a
  * cu_seqlens entry is out of range.  Synchronises the device.  No counterpart

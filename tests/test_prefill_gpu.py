@@ -15,12 +15,18 @@ from oracle import gdn_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def _run(x, in_place=False, cu_dtype=None, scale=None):
+@pytest.fixture(params=["split", "fused"])
+def path(request):
+    """Both prefill paths: the two-stage kernels (default) and the single kernel."""
+    return request.param
+
+
+def _run(x, path="split", in_place=False, cu_dtype=None, scale=None):
     cu = x.cu_seqlens if cu_dtype is None else x.cu_seqlens.to(cu_dtype)
     st = to_dev(x.state)
     out, ns = K.prefill(to_dev(x.q), to_dev(x.k), to_dev(x.v), st, to_dev(x.A_log), to_dev(x.a),
                         to_dev(x.dt_bias), to_dev(x.b), to_dev(cu),
-                        x.scale if scale is None else scale, in_place=in_place)
+                        x.scale if scale is None else scale, in_place=in_place, path=path)
     torch.cuda.synchronize()
     assert _lib.device_status(torch.cuda.current_device()) == 0
     return out.cpu(), ns.cpu()
@@ -43,85 +49,85 @@ def _f(g, n):
 
 
 @pytest.mark.parametrize("tag", ["state", "nostate"])
-def test_prefill_small_golden(tag):
+def test_prefill_small_golden(tag, path):
     """Ragged tails, an empty and a 1-token sequence, int64 cu_seqlens (qk1_v2)."""
     g = _golden(f"prefill_small_{tag}.npz")
     st = _f(g, "state").cuda() if tag == "state" else None
     out, ns = K.prefill(*(_f(g, n).cuda() for n in ("q", "k", "v")), st,
                         *(_f(g, n).cuda() for n in ("A_log", "a", "dt_bias", "b", "cu_seqlens")),
-                        0.0)
+                        0.0, path=path)
     torch.cuda.synchronize()
     assert_prefill_close(out, ns, _f(g, "output"), _f(g, "new_state"), lengths=[37, 0, 129, 1])
 
 
-def test_prefill_full_heads_T150_golden():
+def test_prefill_full_heads_T150_golden(path):
     g = _golden("prefill_qk16v32_T150.npz")
     x = W.make_prefill_inputs([150], seed=3)
-    out, ns = _run(x)
+    out, ns = _run(x, path)
     torch.testing.assert_close(out.float(), _f(g, "output").float(), **PREFILL_OUT_TOL)
     np.testing.assert_allclose(ns[0, 0].numpy(), g["state_head_first"], atol=2e-3, rtol=2e-2)
     np.testing.assert_allclose(ns[-1, -1].numpy(), g["state_head_last"], atol=2e-3, rtol=2e-2)
 
 
 @pytest.mark.parametrize("lengths", [[64], [1], [63], [65], [200], [128, 1, 64, 0, 77]])
-def test_prefill_ragged_lengths(lengths):
+def test_prefill_ragged_lengths(lengths, path):
     x = W.make_prefill_inputs(lengths, seed=sum(lengths) + len(lengths))
-    out, ns = _run(x)
+    out, ns = _run(x, path)
     ro, rs = _oracle(x)
     assert_prefill_close(out, ns, ro, rs, lengths)
 
 
-def test_prefill_varlen_int32_vs_int64_and_in_place():
+def test_prefill_varlen_int32_vs_int64_and_in_place(path):
     lengths = W.varlen_lengths(6, 128, 1024, seed=21)
     x = W.make_prefill_inputs(lengths, seed=21, cu_dtype=torch.int32)
-    o32, s32 = _run(x)
-    o64, s64 = _run(x, cu_dtype=torch.int64)
+    o32, s32 = _run(x, path)
+    o64, s64 = _run(x, path, cu_dtype=torch.int64)
     assert torch.equal(o32, o64) and torch.equal(s32, s64)
-    oi, si = _run(x, in_place=True)
+    oi, si = _run(x, path, in_place=True)
     assert torch.equal(o32, oi) and torch.equal(s32, si)
     ro, rs = _oracle(x)
     assert_prefill_close(o32, s32, ro, rs, lengths)
 
 
-def test_prefill_null_state_and_all_empty():
+def test_prefill_null_state_and_all_empty(path):
     x = W.make_prefill_inputs([100, 0, 30], seed=4, with_state=False)
-    out, ns = _run(x, scale=0.0)
+    out, ns = _run(x, path, scale=0.0)
     ro, rs = _oracle(x)
     assert_prefill_close(out, ns, ro, rs, [100, 0, 30])
     assert ns[1].abs().max().item() == 0.0
     # every sequence empty: states pass through, nothing else is touched
     y = W.make_prefill_inputs([0, 0], seed=5)
-    _, ns2 = _run(y)
+    _, ns2 = _run(y, path)
     assert torch.equal(ns2, y.state)
 
 
 @pytest.mark.parametrize("h_qk,h_v", [(4, 8), (2, 2), (1, 8)])
-def test_prefill_head_layouts(h_qk, h_v):
+def test_prefill_head_layouts(h_qk, h_v, path):
     x = W.make_prefill_inputs([70, 190], seed=8, h_qk=h_qk, h_v=h_v)
-    out, ns = _run(x)
+    out, ns = _run(x, path)
     ro, rs = _oracle(x)
     assert_prefill_close(out, ns, ro, rs)
 
 
-def test_prefill_config2_T8192_drift():
+def test_prefill_config2_T8192_drift(path):
     """one sequence of 8192 tokens, zero initial state; reports drift."""
     x = W.make_prefill_inputs([8192], seed=2, with_state=False)
-    out, ns = _run(x)
+    out, ns = _run(x, path)
     ro, rs = _oracle(x)
     err = assert_prefill_close(out, ns, ro, rs)
     d = (out.float() - ro.float()).abs()
-    print(f"\n[T=8192 drift] output max-abs {d.max().item():.3e} mean-abs {d.mean().item():.3e}; "
+    print(f"\n[T=8192 drift, {path}] output max-abs {d.max().item():.3e} mean-abs {d.mean().item():.3e}; "
           f"final state rel-Frobenius max {err.max().item():.3e}")
 
 
-def test_prefill_config3_varlen16():
+def test_prefill_config3_varlen16(path):
     """16 sequences, lengths U[128, 8192], random initial states, int32."""
     lengths = W.varlen_lengths(16, 128, 8192, seed=3)
     x = W.make_prefill_inputs(lengths, seed=3, cu_dtype=torch.int32)
-    out, ns = _run(x)
+    out, ns = _run(x, path)
     ro, rs = _oracle(x)
     err = assert_prefill_close(out, ns, ro, rs, lengths)
-    print(f"\n[varlen16 drift] per-seq state rel-Frobenius max "
+    print(f"\n[varlen16 drift, {path}] per-seq state rel-Frobenius max "
           f"{[round(float(e), 6) for e in err.max(dim=1).values]}")
 
 
@@ -133,3 +139,31 @@ def test_prefill_rejects_misuse():
     with pytest.raises(ValueError):
         K.prefill(x.q[:, :3], x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
                   x.scale)
+
+
+def test_split_and_fused_paths_agree():
+    """The two paths compute the same products from the same operand tiles."""
+    lengths = [300, 1, 64, 0, 129]
+    x = W.make_prefill_inputs(lengths, seed=12)
+    o1, s1 = _run(x, "split")
+    o2, s2 = _run(x, "fused")
+    assert (o1.float() - o2.float()).abs().max().item() <= 1e-2
+    assert (s1 - s2).abs().max().item() <= 1e-4
+
+
+def test_split_workspace_contract():
+    x = W.make_prefill_inputs([100, 30], seed=6, device="cuda")
+    need = K.prefill_workspace_bytes(2, 130, 32)
+    assert need > 0
+    out = torch.empty(130, 32, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(2, 32, 128, 128, device="cuda")
+    with pytest.raises(ValueError):
+        K.gdn_prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
+                      x.scale, out, ns, workspace=torch.empty(need - 1024, dtype=torch.uint8,
+                                                             device="cuda"))
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    K.gdn_prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale,
+                  out, ns, workspace=ws)
+    ro, rs = O.prefill_chunked(*(t.cpu() for t in (x.q, x.k, x.v, x.state, x.A_log, x.a,
+                                                  x.dt_bias, x.b, x.cu_seqlens)), x.scale)
+    assert_prefill_close(out.cpu(), ns.cpu(), ro, rs)
