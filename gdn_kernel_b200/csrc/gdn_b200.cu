@@ -307,6 +307,76 @@ extern "C" int gdn_b200_prefill_ws(const void* q, const void* k, const void* v,
   return GDN_B200_OK;
 }
 
+// ---------------------------------------------------------------- allocation-free prefill
+// Some callers of this library cannot allocate device memory: a host bound to
+// the reference's fixed `kernel` argument list has no slot to pass a workspace
+// in, a plugin host may own all device memory through its own allocator and
+// forbid raw cudaMalloc, and a latency-critical serving loop may not accept
+// the cost and implicit synchronisation of an allocation on its hot path.
+// gdn_b200_prefill_static serves them from a scratch array that is part of
+// this library's device image: every GPU that loads the library reserves
+// GDN_B200_PREFILL_STATIC_SCRATCH_BYTES for it until the process exits.
+namespace gdn {
+namespace {
+
+static __device__ __align__(256) uint8_t g_prefill_static_scratch[GDN_B200_PREFILL_STATIC_SCRATCH_BYTES];
+
+// Device address of the scratch array, looked up once per device with that
+// device current.  On the host the array's name only stands in for the symbol;
+// it is not a device pointer and must never be passed to a kernel.
+void* g_static_scratch_ptr[kMaxDevices];
+std::mutex g_static_scratch_mu;
+
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(GDN_B200_ERR_CUDA, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_prefill_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(prefill static scratch)");
+    g_static_scratch_ptr[dev] = ptr;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return GDN_B200_OK;
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_b200_prefill_static(const void* q, const void* k, const void* v,
+                                       const float* state, const float* A_log, const void* a,
+                                       const float* dt_bias, const void* b,
+                                       const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                                       double scale, void* output, float* new_state,
+                                       int64_t num_seqs, int64_t total_tokens,
+                                       int32_t num_qk_heads, int32_t num_v_heads,
+                                       int32_t head_dim, void* stream) {
+  t_last_error.clear();
+  if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
+  if (num_seqs < 0 || total_tokens < 0)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0");
+  if (num_seqs == 0) return GDN_B200_OK;
+  const uint64_t need = gdn_b200_prefill_workspace_size(num_seqs, total_tokens, num_v_heads);
+  if (need > GDN_B200_PREFILL_STATIC_SCRATCH_BYTES)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "problem too large for the static prefill scratch: needs " +
+                    std::to_string(need) + " bytes, the limit is " +
+                    std::to_string(static_cast<uint64_t>(GDN_B200_PREFILL_STATIC_SCRATCH_BYTES)) +
+                    " (use gdn_b200_prefill_ws with a caller workspace)");
+  void* scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  // Nothing in the scratch has to start at zero: the chunk-table kernel writes
+  // every table slot the later kernels read, and the prep kernel writes every
+  // record the chain kernel reads, on each call.
+  return gdn_b200_prefill_ws(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64,
+                             scale, output, new_state, num_seqs, total_tokens, num_qk_heads,
+                             num_v_heads, head_dim, scratch, GDN_B200_PREFILL_STATIC_SCRATCH_BYTES,
+                             stream);
+}
+
 extern "C" int gdn_b200_device_status(int32_t device, uint32_t* status, int32_t clear) {
   t_last_error.clear();
   if (!status) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "status is null");

@@ -94,6 +94,34 @@ int gdn_b200_prefill_ws(const void* q, const void* k, const void* v, const float
                         int32_t num_v_heads, int32_t head_dim,
                         void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* Capacity (bytes) of the scratch array that gdn_b200_prefill_static uses. */
+#define GDN_B200_PREFILL_STATIC_SCRATCH_BYTES (64ull << 20)
+
+/*
+ * The two-stage prefill (same arguments, semantics and results as
+ * gdn_b200_prefill_ws) for callers that cannot allocate device memory: hosts
+ * bound to the reference's fixed `kernel` argument list, which has no slot for
+ * a workspace; plugin hosts whose framework owns all device memory and forbids
+ * raw cudaMalloc; and serving loops that cannot afford an allocation on the hot
+ * path.  It allocates nothing: its workspace is a 64 MiB array inside this
+ * library's device image, which every GPU that loads the library holds until
+ * the process exits.  A problem whose gdn_b200_prefill_workspace_size() exceeds
+ * GDN_B200_PREFILL_STATIC_SCRATCH_BYTES is rejected with
+ * GDN_B200_ERR_INVALID_ARGUMENT (with qk16_v32 heads the limit is about 1,300
+ * (64-token chunk, v-head) pairs, i.e. roughly 2,500 packed tokens).
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All calls
+ * on a device share the one array, so calls that overlap on the GPU (other
+ * streams, other host threads) race and corrupt each other's results.
+ * No counterpart in the reference, whose single kernel needs no workspace.
+ */
+int gdn_b200_prefill_static(const void* q, const void* k, const void* v, const float* state,
+                            const float* A_log, const void* a, const float* dt_bias,
+                            const void* b, const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                            double scale, void* output, float* new_state,
+                            int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                            int32_t num_v_heads, int32_t head_dim, void* stream);
+
 /*
  * Reads (and with clear != 0 resets) the status word that the kernels of
  * this library set on `device` when a bounded device-side wait runs out or a
