@@ -301,7 +301,7 @@ extern "C" int gdn_b200_prefill_ws(const void* q, const void* k, const void* v,
     gdn_prefill_prep_kernel<<<g1, kPrefillThreads, kP1Smem, st>>>(tq, tk, sp);
   }
   const dim3 g2(static_cast<unsigned>(2 * num_v_heads), static_cast<unsigned>(num_seqs));
-  gdn_prefill_chain_kernel<<<g2, kPrefillThreads, kC2Smem, st>>>(tk, tv, sp);
+  gdn_prefill_chain_kernel<<<g2, kC2Threads, kC2Smem, st>>>(tk, tv, sp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill (two-stage) launch");
   return GDN_B200_OK;

@@ -63,6 +63,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (up to the hint) instead of re-polling, leaving its sub-partition's
+// issue slots to the warps that work.
+#ifndef GDN_WAIT_HINT_NS
+#define GDN_WAIT_HINT_NS 20000
+#endif
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(GDN_WAIT_HINT_NS)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on the given phase parity.  Returns false when the limit ran
 // out; the caller records an error status and leaves its loop.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
@@ -72,6 +90,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
+}
+
+// Plain arrival (release at CTA scope) by the calling thread.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait that also gives up as soon as another thread of the CTA has
+// raised `abort`, so that one timed-out wait ends every role's loop after at
+// most one more limit.  Returns 1 when the phase completed, 0 when another
+// thread raised `abort`, -1 when this thread's own limit ran out (it then
+// raises `abort`).
+__device__ __forceinline__ int mbar_wait_or_abort(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return 1;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity)) return 1;
+    if (*abort) return 0;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return -1;
+    }
+  }
+}
+
+// One lane of a converged warp (elect.sync); tcgen05.mma and commit are
+// issued by that lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // ---------------------------------------------------------------- proxies
@@ -176,6 +230,13 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   d |= static_cast<uint64_t>(1) << 46;
   d |= static_cast<uint64_t>(2) << 61;
   return d;
+}
+
+// Descriptor of the same operand advanced by `byte_off` bytes (k-steps):
+// adds to the 14-bit start-address field, which cannot carry for shared-memory
+// addresses below 256 KiB.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t byte_off) {
+  return desc + static_cast<uint64_t>(byte_off >> 4);
 }
 
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.

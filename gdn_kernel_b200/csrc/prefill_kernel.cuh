@@ -227,7 +227,9 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
     float x[32];
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
-      float acc = (m == j) ? 1.0f : 0.0f;
+      // four partial sums (one per float4 lane) keep the dependent FMA chain
+      // of each row short; only the newest x enters through the last FMA
+      float acc[4] = {(m == j) ? 1.0f : 0.0f, 0.f, 0.f, 0.f};
       const float4* rp = reinterpret_cast<const float4*>(A + (o + m) * kLdA + o);
 #pragma unroll
       for (int q = 0; q < (m + 3) / 4; ++q) {
@@ -235,9 +237,9 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
         const float av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          if (4 * q + e < m) acc = fmaf(av[e], x[4 * q + e], acc);
+          if (4 * q + e < m) acc[e] = fmaf(av[e], x[4 * q + e], acc[e]);
       }
-      x[m] = acc;
+      x[m] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     }
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
@@ -324,6 +326,23 @@ __device__ __forceinline__ void scale_q_row(uint8_t* tile, int c, float e) {
       __nv_bfloat162 h2 = *reinterpret_cast<__nv_bfloat162*>(&w[q2]);
       float2 f = __bfloat1622float2(h2);
       w[q2] = pack_bf16x2(f.x * e, f.y * e);
+    }
+    *ptr = u;
+  }
+}
+
+// Q'[c] = e Q[c] - pw in place on the 64 columns of one 128-byte row of a
+// K-major swizzled tile (pw: fp32, the same 64 columns).
+__device__ __forceinline__ void qprime_row(uint8_t* tile, int c, float e, const float* pw) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    uint4* ptr = reinterpret_cast<uint4*>(tile + sw128_off(c, cc));
+    uint4 u = *ptr;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int q2 = 0; q2 < 4; ++q2) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[q2]));
+      w[q2] = pack_bf16x2(fmaf(e, f.x, -pw[8 * cc + 2 * q2]), fmaf(e, f.y, -pw[8 * cc + 2 * q2 + 1]));
     }
     *ptr = u;
   }

@@ -6,27 +6,29 @@
 //                            table of (sequence, chunk start, chunk length).
 //   gdn_prefill_prep_kernel  one CTA per (chunk, v-head), two CTAs per SM:
 //                            gates, D_QK = [Q;K]K^T, P and A, the triangular
-//                            inverse, D_W = [T';P]K, then -W and e^gamma Q.  It
-//                            stores the bf16 operand tiles exactly as they sit
-//                            in shared memory (128B-swizzled "tile images"):
-//                            [e^g Q ; -W] (32 KiB), P (8 KiB), T_b (8 KiB), gamma.
-//   gdn_prefill_chain_kernel one CTA per (sequence, v-head, 64-column V slice):
-//                            per chunk, bulk-copies the tile images back into
-//                            shared memory (double-buffered, two chunks ahead),
-//                            and runs
-//                              D_UO  = [Z ; T_b] V_s + [e^g Q ; -W] S_s^T
-//                              v_new = rows 64-127 of D_UO
+//                            inverse (T' = T diag(beta e^gamma), T_b = T diag(beta)),
+//                            D_X = P [T' | T_b], D_W = [T' ; P T'] K.  It folds
+//                            the output's intra-chunk part into two S-free tiles,
+//                              Q' = e^gamma Q - P W      P' = P T_b
+//                            (O = Q' S^T + P' V is e^g Q S^T + P v_new with
+//                            v_new = T_b V - W S^T), and stores the bf16 operand
+//                            tiles exactly as they sit in shared memory
+//                            (128B-swizzled "tile images"): [Q' ; -W] (32 KiB),
+//                            P' (8 KiB), T_b (8 KiB), gamma.
+//   gdn_prefill_chain_kernel one CTA per (sequence, v-head, 64-column V slice),
+//                            warp-specialised; per chunk
+//                              D_UO  = [P' ; T_b] V_s + [Q' ; -W] S_s^T
+//                                      (rows 0-63 output, rows 64-127 v_new)
 //                              D_S4  = K^T (v_new e^{gamma_last-gamma})
-//                              D_UO += [P ; Z] v_new      (rows 0-63: output)
 //                              S_s^T = e^{gamma_last} S_s^T + D_S4
-//                            The output rows of a chunk are written while the
-//                            tensor core already runs the next chunk.
+//                            with only the S-dependent steps serial per chunk.
 //
-// The arithmetic per element is that of the single-kernel path (same operand
-// tiles, same accumulation), so both paths agree with the oracle to the same
-// tolerance.  The workspace holds the tables and one 49 KiB record per
-// (chunk, v-head); it is caller-provided (gdn_b200_prefill_workspace_size),
-// 256-byte aligned (records sit at 1 KiB multiples from its start).
+// Both paths compute the same recurrence with bf16 operands and fp32
+// accumulation and agree with the oracle to the same stated tolerance; the
+// folded tiles Q' and P' round once more to bf16 than the single-kernel path.
+// The workspace holds the tables and one 49 KiB record per (chunk, v-head);
+// it is caller-provided (gdn_b200_prefill_workspace_size), 256-byte aligned
+// (records sit at 1 KiB multiples from its start).
 #pragma once
 
 #include "prefill_kernel.cuh"
@@ -40,8 +42,8 @@ struct ChunkInfo {
 };
 
 // Record of one (chunk, v-head) in the workspace.
-constexpr uint32_t kRecOffQW = 0;          // [e^g Q ; -W] tile image, 32 KiB
-constexpr uint32_t kRecOffP = 32768;       // P tile image, 8 KiB
+constexpr uint32_t kRecOffQW = 0;          // [Q' ; -W] tile image, 32 KiB
+constexpr uint32_t kRecOffP = 32768;       // P' = P T_b tile image, 8 KiB (T_b follows)
 constexpr uint32_t kRecOffTb = 40960;      // T_b tile image, 8 KiB
 constexpr uint32_t kRecOffGam = 49152;     // gamma[64], 256 B
 constexpr uint32_t kRecBytes = 50176;      // 49 KiB (keeps records 1 KiB aligned)
@@ -171,7 +173,8 @@ __device__ __forceinline__ void bulk_commit_and_wait_read() {
 
 // ---------------------------------------------------------------- prep kernel
 constexpr uint32_t kP1OffQKW = 0;                      // 32 KiB [Q;K] then [e^g Q; -W]
-constexpr uint32_t kP1OffTPZT = 32768;                 // 32 KiB T' | P | (unused) | T_b
+constexpr uint32_t kP1OffTPZT = 32768;                 // 32 KiB T' | P, then P T' | P' | T_b
+constexpr uint32_t kP1TbOff = 24576;                   // T_b within that region
 constexpr uint32_t kP1OffAF = 65536;
 constexpr uint32_t kP1OffTF = kP1OffAF + 64 * kLdA * 4;
 constexpr uint32_t kP1OffXS = kP1OffTF + 64 * kLdA * 4;
@@ -180,7 +183,8 @@ constexpr uint32_t kP1OffBar = kP1OffGate + 768;
 constexpr uint32_t kP1OffTmemPtr = kP1OffBar + 16;
 constexpr uint32_t kP1Smem = kP1OffTmemPtr + 16 + 1024;
 constexpr uint32_t kP1TmQK = 0;       // 64 columns
-constexpr uint32_t kP1TmW = 64;       // 128 columns
+constexpr uint32_t kP1TmX = 0;        // 128 columns (D_QK is consumed by then)
+constexpr uint32_t kP1TmW = 128;      // 128 columns
 constexpr uint32_t kP1TmCols = 256;
 
 __global__ void __launch_bounds__(kPrefillThreads, 2)
@@ -263,15 +267,18 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
 
   if (!fail0) {
     // D_QK = [Q ; K] K^T, with K (rows 64-127 of the stacked tile) as the B operand.
-    if (tid == 0) {
-      const uint32_t idesc = idesc_bf16_f32(128, 64, 0, 0);
+    if (warp == 0) {
+      if (elect_one()) {
+        const uint32_t idesc = idesc_bf16_f32(128, 64, 0, 0);
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t koff = (s >> 2) * 16384 + (s & 3) * 32;
-        umma_bf16(tmem + kP1TmQK, sdesc_sw128(a_qkw + koff, 16, 1024),
-                  sdesc_sw128(a_qkw + 8192 + koff, 16, 1024), idesc, s > 0 ? 1u : 0u);
+        for (int s = 0; s < 8; ++s) {
+          const uint32_t koff = (s >> 2) * 16384 + (s & 3) * 32;
+          umma_bf16(tmem + kP1TmQK, sdesc_sw128(a_qkw + koff, 16, 1024),
+                    sdesc_sw128(a_qkw + 8192 + koff, 16, 1024), idesc, s > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_mma);
       }
-      umma_commit(bar_mma);
+      __syncwarp();
     }
     if (!mbar_wait(bar_mma, 0)) code |= kStatusMmaTimeout;
     tc_fence_after();
@@ -280,36 +287,68 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     __syncthreads();
     solve_unit_lower(AF, TF, XS, tpzt, bet, eg, tid);
     fence_proxy_async_smem();
+    tc_fence_before();
     __syncthreads();
-    // D_W = [T' ; P] K, with K as the MN-major B operand (64-column blocks 16 KiB apart).
-    if (tid == 0) {
+    // D_X = [P ; -] [T' | T_b]: P T' (columns 0-63) and P' = P T_b (64-127).
+    // Rows 64-127 of the A operand are scratch; their products are not read.
+    // The B operand's two 64-column blocks are the T' and T_b tiles.
+    if (warp == 0) {
       tc_fence_after();
-      const uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
+      if (elect_one()) {
+        const uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
-        umma_bf16(tmem + kP1TmW, sdesc_sw128(a_tpzt + s * 32, 16, 1024),
-                  sdesc_sw128(a_qkw + 8192 + s * 2048, 16384, 1024), idesc, s > 0 ? 1u : 0u);
-      umma_commit(bar_mma);
+        for (int s = 0; s < 4; ++s)
+          umma_bf16(tmem + kP1TmX, sdesc_sw128(a_tpzt + 8192 + s * 32, 16, 1024),
+                    sdesc_sw128(a_tpzt + s * 2048, kP1TbOff, 1024), idesc, s > 0 ? 1u : 0u);
+        umma_commit(bar_mma);
+      }
+      __syncwarp();
     }
-    if (row < 64) {
+    if (quad < 2) {   // half 0: P T' over P (A rows 64-127 of D_W); half 1: P' to the scratch rows
       if (!mbar_wait(bar_mma, 1)) code |= kStatusMmaTimeout;
       tc_fence_after();
       float r[64];
+      tmem_ld64(tmem + tm_lane + kP1TmX + 64 * half, r);
+      st_row_bf16(tpzt + (half == 0 ? 8192 : 16384), row, r);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // D_W = [T' ; P T'] K, K the MN-major B operand (64-column blocks 16 KiB
+    // apart): rows 0-63 W = T'K, rows 64-127 P W.
+    if (warp == 0) {
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          umma_bf16(tmem + kP1TmW, sdesc_sw128(a_tpzt + s * 32, 16, 1024),
+                    sdesc_sw128(a_qkw + 8192 + s * 2048, 16384, 1024), idesc, s > 0 ? 1u : 0u);
+        umma_commit(bar_mma);
+      }
+      __syncwarp();
+    }
+    if (!mbar_wait(bar_mma, 0)) code |= kStatusMmaTimeout;
+    tc_fence_after();
+    {
+      float r[64];
       tmem_ld64(tmem + tm_lane + kP1TmW + 64 * half, r);
       uint8_t* tile = smem + kP1OffQKW + half * 16384;
-      st_half_row_bf16(tile, 64 + row, 0, r, -1.0f);   // -W over the consumed K rows
-      st_half_row_bf16(tile, 64 + row, 4, r + 32, -1.0f);
-    } else {
-      scale_q_row(smem + kP1OffQKW + half * 16384, row - 64, eg[row - 64]);
+      if (row < 64) {   // -W over the consumed K rows
+        st_half_row_bf16(tile, 64 + row, 0, r, -1.0f);
+        st_half_row_bf16(tile, 64 + row, 4, r + 32, -1.0f);
+      } else {          // Q' = e^gamma Q - P W over the Q rows
+        qprime_row(tile, row - 64, eg[row - 64], r);
+      }
     }
     fence_proxy_async_smem();
     __syncthreads();
-    // Tile images out by bulk copies: [e^g Q ; -W], P, T_b, gamma.
+    // Tile images out by bulk copies: [Q' ; -W], P', T_b, gamma.
     if (tid == 0) {
       uint8_t* rec = sp.records + (static_cast<size_t>(gc) * p.h_v + head) * kRecBytes;
       bulk_store(rec + kRecOffQW, smem + kP1OffQKW, 32768);
-      bulk_store(rec + kRecOffP, tpzt + 8192, 8192);
-      bulk_store(rec + kRecOffTb, tpzt + 24576, 8192);
+      bulk_store(rec + kRecOffP, tpzt + 16384, 8192);
+      bulk_store(rec + kRecOffTb, tpzt + kP1TbOff, 8192);
       bulk_store(rec + kRecOffGam, gam, 256);
       bulk_commit_and_wait_read();
     }
@@ -322,26 +361,60 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
 }
 
 // ---------------------------------------------------------------- chain kernel
-constexpr uint32_t kC2StQW = 0;         // 32 KiB  [e^g Q ; -W]
-constexpr uint32_t kC2StP = 32768;      // 8 KiB   P    } stacked [P ; Z] and [Z ; T_b]
-constexpr uint32_t kC2StZ = 40960;      // 8 KiB   Z    }
-constexpr uint32_t kC2StTb = 49152;     // 8 KiB   T_b  }
-constexpr uint32_t kC2StK = 57344;      // 16 KiB  K chunk [c][kd]
-constexpr uint32_t kC2StV = 73728;      // 8 KiB   V chunk, this CTA's 64 columns [c][v]
-constexpr uint32_t kC2StGam = 81920;    // 256 B   gamma
-constexpr uint32_t kC2Stage = 82944;    // 81 KiB per stage
-constexpr uint32_t kC2OffSB = 2 * kC2Stage;          // 16 KiB S_s^T bf16 [kd][64 v]
-constexpr uint32_t kC2OffVN = kC2OffSB + 16384;      // 8 KiB v_new [c][64 v]
-constexpr uint32_t kC2OffVND = kC2OffVN + 8192;      // 8 KiB decayed v_new
-constexpr uint32_t kC2OffBar = kC2OffVND + 8192;     // 2 load + 2 UMMA barriers
-constexpr uint32_t kC2OffTmemPtr = kC2OffBar + 32;
-constexpr uint32_t kC2Smem = kC2OffTmemPtr + 16 + 1024;
-constexpr uint32_t kC2TmUO = 0;         // 2 x 64 columns (double-buffered)
+// One CTA per (sequence, v-head, 64-column V slice), warp-specialised:
+//   warps 0-7  state warps: thread (k = row, half) keeps S_s^T[k][32 half + j]
+//              in registers; warps 2,3,6,7 also turn rows 64-127 of D_UO into
+//              the decayed v_new tile; warp 0 issues M2 and M3.  The eight
+//              hand over to one another through two named barriers only;
+//   warps 8-9  output warps: rows 0-63 of D_UO -> bf16 output rows;
+//   warp 10    producer: bulk/TMA loads, issued as soon as a stage part frees;
+//   warp 11    M1, and rows past a short chunk's end zeroed once its tiles land.
+// Per chunk c (stage st = c & 1, D_UO double-buffered in TMEM):
+//   M1  D_UO[st]  = [P' ; T_b] V          (warp 11; no S, issued ahead)
+//   M2  D_UO[st] += [Q' ; -W] S_s^T       -> rows 0-63 output, 64-127 v_new
+//   M3  D_S4      = K^T (v_new e^{gamma_last - gamma})
+//   S_s^T = e^{gamma_last} S_s^T + D_S4   (bf16 copy -> M2 of chunk c + 1)
+// Only M2 -> v_new -> M3 -> state update is serial from chunk to chunk.
+constexpr uint32_t kC2StQW = 0;         // 32 KiB [Q' ; -W]  (record)
+constexpr uint32_t kC2StPT = 32768;     // 16 KiB [P' ; T_b] (record, adjacent there too)
+constexpr uint32_t kC2StK = 49152;      // 16 KiB K chunk [c][kd], two 64-column blocks
+constexpr uint32_t kC2StV = 65536;      // 8 KiB  V chunk, this CTA's 64 columns [c][v]
+constexpr uint32_t kC2StGam = 73728;    // 256 B  gamma (record)
+constexpr uint32_t kC2Stage = 74752;    // 73 KiB per stage (1 KiB multiple)
+constexpr uint32_t kC2OffSB = 2 * kC2Stage;        // 16 KiB S_s^T bf16 [kd][64 v]
+constexpr uint32_t kC2OffVND = kC2OffSB + 16384;   // 8 KiB decayed v_new [c][64 v]
+constexpr uint32_t kC2OffBar = kC2OffVND + 8192;
+// mbarriers (pairs are per stage / D_UO buffer):
+//   LdA, LdB   stage loads landed (record + V; K)
+//   M1         M1 done (loader's commit)          UO    M2 done (warp 0's commit)
+//   Out        output warps have read D_UO[st]    FreeA / FreeB  stage parts reusable
+//   KReady     K landed and short rows zeroed     S     M3 done
+//   End, End2  drains of an aborted run (warp 0, warp 11)
+enum : int {
+  kC2BarLdA = 0, kC2BarLdB = 2, kC2BarM1 = 4, kC2BarUO = 6, kC2BarOut = 8,
+  kC2BarFreeA = 10, kC2BarFreeB = 12, kC2BarKReady = 14, kC2BarS = 16, kC2BarEnd = 17,
+  kC2BarEnd2 = 18, kC2NumBars = 19
+};
+constexpr uint32_t kC2OffTmemPtr = kC2OffBar + 8 * kC2NumBars;
+constexpr uint32_t kC2OffAbort = kC2OffTmemPtr + 16;
+constexpr uint32_t kC2Smem = kC2OffAbort + 16 + 1024;
+constexpr uint32_t kC2TmUO = 0;         // 2 x 64 columns
 constexpr uint32_t kC2TmS4 = 128;       // 64 columns
 constexpr uint32_t kC2TmCols = 256;
-constexpr uint32_t kC2LoadBytes = 32768 + 8192 + 8192 + 256 + 16384 + 8192;
+constexpr uint32_t kC2LoadA = 32768 + 16384 + 8192 + 256;
+constexpr uint32_t kC2LoadB = 16384;
+constexpr int kC2StateWarps = 8;
+constexpr int kC2OutWarps = 2;
+constexpr int kC2LoaderWarp = kC2StateWarps + kC2OutWarps;
+constexpr int kC2M1Warp = kC2LoaderWarp + 1;
+constexpr int kC2Threads = 32 * (kC2M1Warp + 1);
 
-__global__ void __launch_bounds__(kPrefillThreads, 1)
+// Named barrier among the state warps (ids 1, 2; 0 is __syncthreads).
+__device__ __forceinline__ void state_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(32 * kC2StateWarps) : "memory");
+}
+
+__global__ void __launch_bounds__(kC2Threads, 1)
     gdn_prefill_chain_kernel(const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const SplitParams sp) {
   extern __shared__ uint8_t smem_raw[];
@@ -351,7 +424,6 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   const int head = blockIdx.x >> 1, vs = blockIdx.x & 1, seq = blockIdx.y;
   const int hq = head / (p.h_v / p.h_qk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, half = warp >> 2, row = quad * 32 + lane;
   const int gc0 = sp.seq_off[seq];
   const int nch = sp.seq_off[seq + 1] - gc0;
   // this CTA's slice: state rows v in [64 vs, 64 vs + 64)
@@ -361,211 +433,284 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   if (nch <= 0) {   // ref kernel_prefill.cu:61-66: the state passes through unchanged
     float4* dst = reinterpret_cast<float4*>(p.new_state + sbase);
     const float4* src = p.state ? reinterpret_cast<const float4*>(p.state + sbase) : nullptr;
-    for (int i = tid; i < 64 * kHeadDim / 4; i += kPrefillThreads)
+    for (int i = tid; i < 64 * kHeadDim / 4; i += kC2Threads)
       dst[i] = src ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     return;
   }
+  // Chunks of one sequence are consecutive 64-token windows; only the last
+  // may be short.
+  const long long cstart0 = sp.table[gc0].cstart;
+  const int clen_last = sp.table[gc0 + nch - 1].clen;
+  auto chunk_len = [&](int c) { return c == nch - 1 ? clen_last : kChunk; };
 
-  uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + kC2OffBar);   // [2]
-  uint64_t* bar_mma = bar_ld + 2;
-  uint64_t* bar_mma2 = bar_ld + 3;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kC2OffBar);
   uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + kC2OffTmemPtr);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kC2OffAbort);
 
-  auto issue_loads = [&](int ci) {   // stage ci & 1 <- chunk ci of this sequence
-    const int st = ci & 1;
+  auto load_a = [&](int c) {   // record tiles + V of chunk c -> stage c & 1
+    const int st = c & 1;
     uint8_t* stage = smem + st * kC2Stage;
-    const int gc = gc0 + ci;
-    const ChunkInfo info = sp.table[gc];
-    const uint8_t* rec = sp.records + (static_cast<size_t>(gc) * p.h_v + head) * kRecBytes;
-    mbar_arrive_expect_tx(bar_ld + st, kC2LoadBytes);
-    bulk_load(stage + kC2StQW, rec + kRecOffQW, 32768, bar_ld + st);
-    bulk_load(stage + kC2StP, rec + kRecOffP, 8192, bar_ld + st);
-    bulk_load(stage + kC2StTb, rec + kRecOffTb, 8192, bar_ld + st);
-    bulk_load(stage + kC2StGam, rec + kRecOffGam, 256, bar_ld + st);
-    const int t0 = static_cast<int>(info.cstart);
-    tma_load_3d(stage + kC2StK, &tm_k, bar_ld + st, 0, hq, t0);
-    tma_load_3d(stage + kC2StK + 8192, &tm_k, bar_ld + st, 64, hq, t0);
-    tma_load_3d(stage + kC2StV, &tm_v, bar_ld + st, 64 * vs, head, t0);
+    uint64_t* bar = bars + kC2BarLdA + st;
+    const uint8_t* rec =
+        sp.records + (static_cast<size_t>(gc0 + c) * p.h_v + head) * kRecBytes;
+    mbar_arrive_expect_tx(bar, kC2LoadA);
+    bulk_load(stage + kC2StQW, rec + kRecOffQW, 32768, bar);
+    bulk_load(stage + kC2StPT, rec + kRecOffP, 16384, bar);
+    bulk_load(stage + kC2StGam, rec + kRecOffGam, 256, bar);
+    tma_load_3d(stage + kC2StV, &tm_v, bar, 64 * vs, head, static_cast<int>(cstart0 + 64 * c));
+  };
+  auto load_b = [&](int c) {   // K of chunk c -> stage c & 1
+    const int st = c & 1;
+    uint8_t* stage = smem + st * kC2Stage;
+    uint64_t* bar = bars + kC2BarLdB + st;
+    const int t0 = static_cast<int>(cstart0 + 64 * c);
+    mbar_arrive_expect_tx(bar, kC2LoadB);
+    tma_load_3d(stage + kC2StK, &tm_k, bar, 0, hq, t0);
+    tma_load_3d(stage + kC2StK + 8192, &tm_k, bar, 64, hq, t0);
   };
 
   if (warp == 0) {
     tmem_alloc(tmem_ptr, kC2TmCols);
     tmem_relinquish();
   }
-  if (tid == 32) {
-    for (int i = 0; i < 4; ++i) mbar_init(bar_ld + i, 1);
+  if (warp == kC2LoaderWarp && lane == 0) {
+    *abort_flag = 0;
+    for (int i = 0; i < kC2NumBars; ++i)
+      mbar_init(bars + i, (i == kC2BarOut || i == kC2BarOut + 1) ? kC2OutWarps : 1);
     fence_mbarrier_init();
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
+    load_a(0);
+    load_b(0);
+    if (nch > 1) {
+      load_a(1);
+      load_b(1);
+    }
   }
-  for (int i = tid; i < 512; i += kPrefillThreads) {   // Z blocks of both stages
-    reinterpret_cast<uint4*>(smem + kC2StZ)[i] = make_uint4(0, 0, 0, 0);
-    reinterpret_cast<uint4*>(smem + kC2Stage + kC2StZ)[i] = make_uint4(0, 0, 0, 0);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    issue_loads(0);
-    if (nch > 1) issue_loads(1);
-  }
-  // Thread (k = row, half) holds S_s^T[k][32 half + j] = S[64 vs + 32 half + j][k].
   float sreg[32];
+  const int quad = warp & 3, half = (warp >> 2) & 1, row = quad * 32 + lane;
+  if (warp < kC2StateWarps) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j)
-    sreg[j] = p.state ? p.state[sbase + static_cast<size_t>(32 * half + j) * kHeadDim + row] : 0.f;
-  st_half_row_bf16(smem + kC2OffSB, row, 4 * half, sreg, 1.0f);
-  fence_proxy_async_smem();
+    for (int j = 0; j < 32; ++j)
+      sreg[j] =
+          p.state ? p.state[sbase + static_cast<size_t>(32 * half + j) * kHeadDim + row] : 0.f;
+    st_half_row_bf16(smem + kC2OffSB, row, 4 * half, sreg, 1.0f);
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_ptr;
   const uint32_t tm_lane = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t a_sb = smem_u32(smem + kC2OffSB);
-  const uint32_t a_vn = smem_u32(smem + kC2OffVN);
-  const uint32_t a_vnd = smem_u32(smem + kC2OffVND);
+  const uint32_t idesc_uo = idesc_bf16_f32(128, 64, 0, 1);
 
-  bool failed = false;
-  unsigned int fail_code = 0;
-  auto wait = [&](uint64_t* bar, uint32_t parity, unsigned int code) {
-    if (!mbar_wait(bar, parity)) {
-      failed = true;
-      fail_code |= code;
-    }
+  // Waits are warp-uniform: every lane polls, and the warp proceeds only if
+  // all saw the phase complete (a limit that runs out mid-warp cannot split it).
+  auto warp_wait = [&](int bar, uint32_t parity, unsigned int code) {
+    const int r = mbar_wait_or_abort(bars + bar, parity, abort_flag);
+    if (r < 0) atomicOr(p.status, code);
+    return __all_sync(0xffffffffu, r == 1);
   };
-  // bar_mma completes twice per chunk (parity 0: U + S^T products, parity 1:
-  // state increment); bar_mma2 once per chunk (the P v_new product, parity =
-  // chunk & 1); bar_ld[stage] once per use of the stage (parity = (chunk >> 1) & 1).
-  auto output_rows = [&](int cj) {   // rows 0-63 of D_UO of chunk cj -> output
-    wait(bar_mma2, cj & 1, kStatusMmaTimeout);
-    tc_fence_after();
-    const ChunkInfo info = sp.table[gc0 + cj];
-    float r[32];
-    tmem_ld32(tmem + kC2TmUO + 64 * (cj & 1) + tm_lane + 32 * half, r);
-    tmem_wait_ld();
-    if (row < info.clen) {
-      __nv_bfloat16* orow = p.out + (static_cast<size_t>(info.cstart + row) * p.h_v + head) *
-                                        kHeadDim + 64 * vs + 32 * half;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint4 u;
-        u.x = pack_bf16x2(p.scale * r[8 * cc + 0], p.scale * r[8 * cc + 1]);
-        u.y = pack_bf16x2(p.scale * r[8 * cc + 2], p.scale * r[8 * cc + 3]);
-        u.z = pack_bf16x2(p.scale * r[8 * cc + 4], p.scale * r[8 * cc + 5]);
-        u.w = pack_bf16x2(p.scale * r[8 * cc + 6], p.scale * r[8 * cc + 7]);
-        *reinterpret_cast<uint4*>(orow + 8 * cc) = u;
+  // Drain of an aborted run: the tensor-core ops this warp issued land
+  // before the CTA's TMEM and shared memory go away.
+  auto drain_mma = [&](int bar) {
+    if (elect_one()) umma_commit(bars + bar);
+    __syncwarp();
+    mbar_wait(bars + bar, 0);
+  };
+
+  if (warp == kC2LoaderWarp) {
+    // ------------------------------------------------ producer warp
+    // Stage parts are refilled as soon as chunk c - 2 releases them (its M1,
+    // M2 and gamma reads for part A, its M3 for part B).
+    int issued = nch > 1 ? 2 : 1;
+    bool ok = true;
+    for (int c = 2; c < nch; ++c) {
+      const int st = c & 1;
+      if (!(ok = warp_wait(kC2BarFreeA + st, ((c - 2) >> 1) & 1, kStatusMmaTimeout))) break;
+      if (elect_one()) load_a(c);
+      __syncwarp();
+      if (!(ok = warp_wait(kC2BarFreeB + st, ((c - 2) >> 1) & 1, kStatusMmaTimeout))) {
+        issued = c + 1;   // part A of chunk c is in flight
+        if (elect_one()) mbar_arrive_expect_tx(bars + kC2BarLdB + st, 0);   // nothing for B
+        __syncwarp();
+        break;
+      }
+      if (elect_one()) load_b(c);
+      __syncwarp();
+      issued = c + 1;
+    }
+    if (!ok) {
+      // Aborted: the copies of the last two issued chunks land first (each
+      // wait bounded on its own; a landed phase reads as complete).
+      for (int c = issued > 2 ? issued - 2 : 0; c < issued; ++c) {
+        mbar_wait(bars + kC2BarLdA + (c & 1), (c >> 1) & 1);
+        mbar_wait(bars + kC2BarLdB + (c & 1), (c >> 1) & 1);
       }
     }
-  };
-  auto stage_ready = [&](int cj) {   // wait for chunk cj's tiles; clear rows past its end
-    const int sj = cj & 1;
-    wait(bar_ld + sj, (cj >> 1) & 1, kStatusTmaTimeout);
-    const int clen = sp.table[gc0 + cj].clen;
-    if (clen < kChunk) {
-      uint8_t* stage = smem + sj * kC2Stage;
+  } else if (warp == kC2M1Warp) {
+    // ------------------------------------------------ M1 warp
+    bool ok = true;
+    // Rows past the sequence end of a short chunk's tile (they hold the next
+    // sequence's tokens): zero them before a tensor-core read.
+    auto zero_rows = [&](uint8_t* tile, int nblk, int clen) {
       const int nrow = kChunk - clen;
-      for (int e = tid; e < 3 * nrow * 8; e += kPrefillThreads) {
-        const int reg = e / (nrow * 8);
-        const int r = clen + (e / 8) % nrow;
-        const uint32_t base = reg < 2 ? kC2StK + reg * 8192 : kC2StV;
-        *reinterpret_cast<uint4*>(stage + base + sw128_off(r, e & 7)) = make_uint4(0, 0, 0, 0);
+      for (int e = lane; e < nblk * nrow * 8; e += 32) {
+        const int blk = e / (nrow * 8);
+        const int r = clen + (e >> 3) % nrow;
+        *reinterpret_cast<uint4*>(tile + blk * 8192 + sw128_off(r, e & 7)) =
+            make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async_smem();
-    }
-  };
-
-  stage_ready(0);
-  __syncthreads();
-  for (int ci = 0; ci < nch; ++ci) {
-    const int st = ci & 1;
-    uint8_t* stage = smem + st * kC2Stage;
-    const uint32_t a_stage = smem_u32(stage);
-    const int clen = sp.table[gc0 + ci].clen;
-    const uint32_t d_uo = tmem + kC2TmUO + 64 * st;
-    const float* gam = reinterpret_cast<const float*>(stage + kC2StGam);
-
-    // D_UO = [Z ; T_b] V_s + [e^g Q ; -W] S_s^T
-    if (tid == 0) {
+      __syncwarp();
+    };
+    for (int c = 0; c < nch; ++c) {
+      const int st = c & 1;
+      uint8_t* stage = smem + st * kC2Stage;
+      const int clen = chunk_len(c);
+      if (!(ok = warp_wait(kC2BarLdA + st, (c >> 1) & 1, kStatusTmaTimeout))) break;
+      if (clen < kChunk) zero_rows(stage + kC2StV, 1, clen);
+      // M1 into D_UO[st] once the output warps have read its chunk c - 2
+      if (c >= 2 && !(ok = warp_wait(kC2BarOut + st, ((c - 2) >> 1) & 1, kStatusMmaTimeout)))
+        break;
       tc_fence_after();
-      const uint32_t idesc = idesc_bf16_f32(128, 64, 0, 1);
+      if (elect_one()) {
+        const uint32_t a_st = smem_u32(stage);
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
-        umma_bf16(d_uo, sdesc_sw128(a_stage + kC2StZ + s * 32, 16, 1024),
-                  sdesc_sw128(a_stage + kC2StV + s * 2048, 8192, 1024), idesc, s > 0 ? 1u : 0u);
+        for (int s = 0; s < 4; ++s)
+          umma_bf16(tmem + kC2TmUO + 64 * st, sdesc_sw128(a_st + kC2StPT + s * 32, 16, 1024),
+                    sdesc_sw128(a_st + kC2StV + s * 2048, 8192, 1024), idesc_uo,
+                    s > 0 ? 1u : 0u);
+        umma_commit(bars + kC2BarM1 + st);
+      }
+      __syncwarp();
+      if (!(ok = warp_wait(kC2BarLdB + st, (c >> 1) & 1, kStatusTmaTimeout))) break;
+      if (clen < kChunk) zero_rows(stage + kC2StK, 2, clen);
+      if (elect_one()) mbar_arrive(bars + kC2BarKReady + st);
+      __syncwarp();
+    }
+    if (!ok) drain_mma(kC2BarEnd2);
+  } else if (warp < kC2StateWarps) {
+    // ------------------------------------------------ state warps
+    // Every state warp runs all nch iterations and reaches both named
+    // barriers each time, also after a failed wait (the work is then
+    // skipped): a warp that left early would strand the others there.
+    const uint32_t a_sb = smem_u32(smem + kC2OffSB);
+    const uint32_t a_vnd = smem_u32(smem + kC2OffVND);
+    const uint32_t idesc_s = idesc_bf16_f32(128, 64, 1, 1);
+    bool ok = true;
+    for (int c = 0; c < nch; ++c) {
+      const int st = c & 1;
+      const uint8_t* stage = smem + st * kC2Stage;
+      const uint32_t a_st = smem_u32(stage);
+      const int clen = chunk_len(c);
+      ok = ok && warp_wait(kC2BarLdA + st, (c >> 1) & 1, kStatusTmaTimeout);
+      float gam_last = 0.f, dec = 0.f;
+      if (ok) {
+        const float* gam = reinterpret_cast<const float*>(stage + kC2StGam);
+        gam_last = gam[clen - 1];
+        const int cc = row - 64;
+        if (quad >= 2 && cc < clen) dec = __expf(gam_last - gam[cc]);
+      }
+      if (warp == 0) {   // M2, after M1 of this chunk
+        ok = ok && warp_wait(kC2BarM1 + st, (c >> 1) & 1, kStatusMmaTimeout);
+        if (ok) {
+          tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-      for (int s = 0; s < 8; ++s)
-        umma_bf16(d_uo, sdesc_sw128(a_stage + kC2StQW + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
-                  sdesc_sw128(a_sb + s * 2048, 16384, 1024), idesc, 1u);
-      umma_commit(bar_mma);
-    }
-    // the previous chunk's output rows, while the tensor core works on this one
-    if (row < 64 && ci > 0) output_rows(ci - 1);
-    wait(bar_mma, 0, kStatusMmaTimeout);
-    tc_fence_after();
-
-    const float gam_last = gam[clen - 1];
-    if (row >= 64) {   // v_new rows
-      const int c = row - 64;
-      const float dec = (c < clen) ? __expf(gam_last - gam[c]) : 0.f;
-      const float keep = (c < clen) ? 1.f : 0.f;
-      float r[32];
-      tmem_ld32(d_uo + tm_lane + 32 * half, r);
-      tmem_wait_ld();
-      st_half_row_bf16(smem + kC2OffVN, c, 4 * half, r, keep);
-      st_half_row_bf16(smem + kC2OffVND, c, 4 * half, r, dec);
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-
-    // D_S4 = K^T (v_new e^{gamma_last - gamma});  D_UO += [P ; Z] v_new
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t idesc_s = idesc_bf16_f32(128, 64, 1, 1);
-      const uint32_t idesc_o = idesc_bf16_f32(128, 64, 0, 1);
+            for (int s = 0; s < 8; ++s)
+              umma_bf16(tmem + kC2TmUO + 64 * st,
+                        sdesc_sw128(a_st + kC2StQW + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
+                        sdesc_sw128(a_sb + s * 2048, 16384, 1024), idesc_uo, 1u);
+            umma_commit(bars + kC2BarUO + st);
+          }
+          __syncwarp();
+        }
+      }
+      if (quad >= 2) {   // v_new rows -> decayed v_new tile
+        ok = ok && warp_wait(kC2BarUO + st, (c >> 1) & 1, kStatusMmaTimeout);
+        if (ok) {
+          tc_fence_after();
+          float r[32];
+          tmem_ld32(tmem + kC2TmUO + 64 * st + tm_lane + 32 * half, r);
+          tmem_wait_ld();
+          st_half_row_bf16(smem + kC2OffVND, row - 64, 4 * half, r, dec);
+          fence_proxy_async_smem();
+        }
+      }
+      tc_fence_before();
+      state_sync(1);
+      if (warp == 0) {   // M3, once K is in; the record part of the stage is free
+        if (ok && elect_one()) mbar_arrive(bars + kC2BarFreeA + st);
+        __syncwarp();
+        ok = ok && warp_wait(kC2BarKReady + st, (c >> 1) & 1, kStatusTmaTimeout);
+        if (ok) {
+          tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
-        umma_bf16(tmem + kC2TmS4, sdesc_sw128(a_stage + kC2StK + s * 2048, 8192, 1024),
-                  sdesc_sw128(a_vnd + s * 2048, 8192, 1024), idesc_s, s > 0 ? 1u : 0u);
-      umma_commit(bar_mma);
+            for (int s = 0; s < 4; ++s)
+              umma_bf16(tmem + kC2TmS4, sdesc_sw128(a_st + kC2StK + s * 2048, 8192, 1024),
+                        sdesc_sw128(a_vnd + s * 2048, 8192, 1024), idesc_s, s > 0 ? 1u : 0u);
+            umma_commit(bars + kC2BarS);
+          }
+          __syncwarp();
+        }
+      }
+      ok = ok && warp_wait(kC2BarS, c & 1, kStatusMmaTimeout);
+      if (ok) {   // S_s^T = e^{gamma_last} S_s^T + D_S4
+        if (warp == 0) {
+          if (elect_one()) mbar_arrive(bars + kC2BarFreeB + st);
+          __syncwarp();
+        }
+        tc_fence_after();
+        const float decay = __expf(gam_last);
+        float r[32];
+        tmem_ld32(tmem + kC2TmS4 + tm_lane + 32 * half, r);
+        tmem_wait_ld();
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
-        umma_bf16(d_uo, sdesc_sw128(a_stage + kC2StP + s * 32, 16, 1024),
-                  sdesc_sw128(a_vn + s * 2048, 8192, 1024), idesc_o, 1u);
-      umma_commit(bar_mma2);
+        for (int j = 0; j < 32; ++j) sreg[j] = fmaf(decay, sreg[j], r[j]);
+        st_half_row_bf16(smem + kC2OffSB, row, 4 * half, sreg, 1.0f);
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      state_sync(2);
     }
-    wait(bar_mma, 1, kStatusMmaTimeout);
-    tc_fence_after();
-    {   // S_s^T = e^{gamma_last} S_s^T + D_S4
-      const float decay = __expf(gam_last);
-      float r[32];
-      tmem_ld32(tmem + tm_lane + kC2TmS4 + 32 * half, r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sreg[j] = fmaf(decay, sreg[j], r[j]);
-      st_half_row_bf16(smem + kC2OffSB, row, 4 * half, sreg, 1.0f);
-    }
-    if (tid == 0 && ci + 2 < nch) {
-      // stage `st` is free once the P v_new product (its last reader) is done
-      wait(bar_mma2, ci & 1, kStatusMmaTimeout);
-      issue_loads(ci + 2);
-    }
-    if (ci + 1 < nch) stage_ready(ci + 1);
-    fence_proxy_async_smem();
-    tc_fence_before();
-    if (__syncthreads_or(failed)) break;
-  }
-  bool any_fail = __syncthreads_or(failed);
-  if (!any_fail && row < 64) output_rows(nch - 1);
-  any_fail = __syncthreads_or(failed);
-  if (any_fail) {
-    if (failed) atomicOr(p.status, fail_code);
+    if (warp == 0 && *abort_flag) drain_mma(kC2BarEnd);
   } else {
+    // ------------------------------------------------ output warps (TMEM lanes 0-63)
+    const int orow = (warp - kC2StateWarps) * 32 + lane;
+    for (int c = 0; c < nch; ++c) {
+      const int st = c & 1;
+      if (!warp_wait(kC2BarUO + st, (c >> 1) & 1, kStatusMmaTimeout)) break;
+      tc_fence_after();
+      float r[64];
+      tmem_ld64(tmem + kC2TmUO + 64 * st + tm_lane, r);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars + kC2BarOut + st);
+      if (orow < chunk_len(c)) {
+        __nv_bfloat16* o = p.out + (static_cast<size_t>(cstart0 + 64 * c + orow) * p.h_v + head) *
+                                       kHeadDim + 64 * vs;
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      p.new_state[sbase + static_cast<size_t>(32 * half + j) * kHeadDim + row] = sreg[j];
+        for (int cc = 0; cc < 8; ++cc) {
+          uint4 u;
+          u.x = pack_bf16x2(p.scale * r[8 * cc + 0], p.scale * r[8 * cc + 1]);
+          u.y = pack_bf16x2(p.scale * r[8 * cc + 2], p.scale * r[8 * cc + 3]);
+          u.z = pack_bf16x2(p.scale * r[8 * cc + 4], p.scale * r[8 * cc + 5]);
+          u.w = pack_bf16x2(p.scale * r[8 * cc + 6], p.scale * r[8 * cc + 7]);
+          *reinterpret_cast<uint4*>(o + 8 * cc) = u;
+        }
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (!*abort_flag && warp < kC2StateWarps) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      p.new_state[sbase + static_cast<size_t>(32 * half + j) * kHeadDim + row] = sreg[j];
+  }
   if (warp == 0) tmem_dealloc(tmem, kC2TmCols);
 }
 
