@@ -224,15 +224,18 @@ def time_prefill(K, lengths, iters, warmup, flush, seed=0, with_state=True):
     out = torch.empty(T, H_V, D, dtype=torch.bfloat16, device="cuda")
     ns = torch.empty(len(lengths), H_V, D, D, dtype=torch.float32, device="cuda")
     args = (x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale, out, ns)
+    # the two-stage path's workspace is allocated once, outside the timed region
+    ws = torch.empty(K.prefill_workspace_bytes(len(lengths), T, H_V), dtype=torch.uint8,
+                     device="cuda")
     for _ in range(warmup):
         flush.zero_()
-        K.gdn_prefill(*args)
+        K.gdn_prefill(*args, workspace=ws)
     torch.cuda.synchronize()
     ev = [_events() for _ in range(iters)]
     for e0, e1 in ev:
         flush.zero_()
         e0.record()
-        K.gdn_prefill(*args)
+        K.gdn_prefill(*args, workspace=ws)
         e1.record()
     torch.cuda.synchronize()
     return [e0.elapsed_time(e1) for e0, e1 in ev]
