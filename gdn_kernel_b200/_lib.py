@@ -24,6 +24,7 @@ GDN_B200_ERR_CUDA = 2
 STATUS_TMA_TIMEOUT = 1
 STATUS_MMA_TIMEOUT = 2
 STATUS_BAD_SEQLENS = 4
+STATUS_BAD_INDEX = 8
 
 # Every symbol the header declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -31,6 +32,10 @@ _SIGNATURES = {
     "gdn_b200_decode": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_double, _P, _P,
                                        ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _P]),
+    "gdn_b200_decode_pool": (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_int32, _P, _P,
+                                            ctypes.c_int32, _P, _P, _P, _P, _P, ctypes.c_double,
+                                            _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P]),
     "gdn_b200_prefill": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int32,
                                         ctypes.c_double, _P, _P, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P]),

@@ -12,6 +12,7 @@
 
 #include "gdn_b200.h"
 #include "decode_kernel.cuh"
+#include "decode_pool_kernel.cuh"
 #include "prefill_split.cuh"
 
 namespace gdn {
@@ -168,6 +169,68 @@ extern "C" int gdn_b200_decode(const void* q, const void* k, const void* v, cons
     gdn_decode_kernel<false><<<grid, kDecodeThreads, 0, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return GDN_B200_OK;
+}
+
+extern "C" int gdn_b200_decode_pool(const void* q, const void* k, const void* v,
+                                    const void* state_pool, void* new_state_pool,
+                                    int32_t state_is_bf16, const void* read_indices,
+                                    const void* write_indices, int32_t indices_are_int64,
+                                    void* intermediate_states, const float* A_log, const void* a,
+                                    const float* dt_bias, const void* b, double scale,
+                                    void* output, int64_t batch, int64_t seq_len,
+                                    int64_t pool_size, int32_t num_qk_heads, int32_t num_v_heads,
+                                    int32_t head_dim, void* stream) {
+  t_last_error.clear();
+  if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
+  if (batch < 0) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch must be >= 0");
+  if (seq_len < 1 || seq_len > 0x7fffffffLL)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "seq_len must be in [1, 2^31)");
+  if (batch * num_v_heads * (kHeadDim / 16) > 0x7fffffffLL)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch * num_v_heads exceeds the grid limit");
+  if (batch == 0) return GDN_B200_OK;
+  if (pool_size < 1) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "pool_size must be >= 1");
+  if (!q || !k || !v || !state_pool || !new_state_pool || !read_indices || !A_log || !a ||
+      !dt_bias || !b || !output)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const int state_align = state_is_bf16 ? 8 : 16;
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(state_pool, state_align) ||
+      !aligned(new_state_pool, state_align) ||
+      (intermediate_states && !aligned(intermediate_states, state_align)))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "q/k need 8-byte alignment and the state buffers 16-byte (fp32) or "
+                "8-byte (bf16) alignment");
+  unsigned int* status = nullptr;
+  if (int rc = device_setup(&status)) return rc;
+  PoolDecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.pool = state_pool;
+  p.new_pool = new_state_pool;
+  p.inter = intermediate_states;
+  p.read_idx = read_indices;
+  p.write_idx = write_indices;
+  p.idx_is_int64 = indices_are_int64 ? 1 : 0;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.scale = resolve_scale(scale);
+  p.out = static_cast<__nv_bfloat16*>(output);
+  p.status = status;
+  p.pool_size = pool_size;
+  p.T = static_cast<int>(seq_len);
+  p.h_qk = num_qk_heads;
+  p.h_v = num_v_heads;
+  const dim3 grid(static_cast<unsigned>(batch * num_v_heads * (kHeadDim / 16)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (state_is_bf16)
+    gdn_decode_pool_kernel<__nv_bfloat16><<<grid, kDecodeThreads, 0, st>>>(p);
+  else
+    gdn_decode_pool_kernel<float><<<grid, kDecodeThreads, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "pooled decode launch");
   return GDN_B200_OK;
 }
 
@@ -400,4 +463,4 @@ extern "C" int gdn_b200_device_status(int32_t device, uint32_t* status, int32_t 
 
 extern "C" const char* gdn_b200_last_error(void) { return t_last_error.c_str(); }
 
-extern "C" int32_t gdn_b200_abi_version(void) { return 100; }
+extern "C" int32_t gdn_b200_abi_version(void) { return 101; }

@@ -186,6 +186,29 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// The same UMMA issued by one elected lane of a converged warp: every lane
+// executes the instruction sequence, only the elected one issues, and the warp
+// never diverges (no reconvergence after the issue).
+__device__ __forceinline__ void umma_bf16_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
 // Arrive on an mbarrier once every previously issued tcgen05 op of this thread completes.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(

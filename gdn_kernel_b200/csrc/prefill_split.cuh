@@ -599,33 +599,36 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     const uint32_t a_vnd = smem_u32(smem + kC2OffVND);
     const uint32_t idesc_s = idesc_bf16_f32(128, 64, 1, 1);
     bool ok = true;
+    // Waits on phases that are normally long complete sit in idle slots of
+    // the previous step, off the chain: the gammas of chunk c + 1 and (warp 0)
+    // M1 of chunk c + 1 while M3 of chunk c runs, K of chunk c while the
+    // v_new epilogue runs.
+    float gam_last = 0.f, dec = 0.f;
+    auto gammas = [&](int c) {   // chunk c's gamma_last and this row's v_new decay
+      ok = ok && warp_wait(kC2BarLdA + (c & 1), (c >> 1) & 1, kStatusTmaTimeout);
+      if (ok) {
+        const float* gam = reinterpret_cast<const float*>(smem + (c & 1) * kC2Stage + kC2StGam);
+        const int clen = chunk_len(c), cc = row - 64;
+        gam_last = gam[clen - 1];
+        dec = (quad >= 2 && cc < clen) ? __expf(gam_last - gam[cc]) : 0.f;
+      }
+    };
+    gammas(0);
+    if (warp == 0) ok = ok && warp_wait(kC2BarM1, 0, kStatusMmaTimeout);
     for (int c = 0; c < nch; ++c) {
       const int st = c & 1;
-      const uint8_t* stage = smem + st * kC2Stage;
-      const uint32_t a_st = smem_u32(stage);
-      const int clen = chunk_len(c);
-      ok = ok && warp_wait(kC2BarLdA + st, (c >> 1) & 1, kStatusTmaTimeout);
-      float gam_last = 0.f, dec = 0.f;
-      if (ok) {
-        const float* gam = reinterpret_cast<const float*>(stage + kC2StGam);
-        gam_last = gam[clen - 1];
-        const int cc = row - 64;
-        if (quad >= 2 && cc < clen) dec = __expf(gam_last - gam[cc]);
-      }
-      if (warp == 0) {   // M2, after M1 of this chunk
-        ok = ok && warp_wait(kC2BarM1 + st, (c >> 1) & 1, kStatusMmaTimeout);
+      const uint32_t a_st = smem_u32(smem + st * kC2Stage);
+      if (warp == 0) {   // M2 (M1 of this chunk is complete), then K of this chunk
         if (ok) {
           tc_fence_after();
-          if (elect_one()) {
 #pragma unroll
-            for (int s = 0; s < 8; ++s)
-              umma_bf16(tmem + kC2TmUO + 64 * st,
-                        sdesc_sw128(a_st + kC2StQW + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
-                        sdesc_sw128(a_sb + s * 2048, 16384, 1024), idesc_uo, 1u);
-            umma_commit(bars + kC2BarUO + st);
-          }
-          __syncwarp();
+          for (int s = 0; s < 8; ++s)
+            umma_bf16_elect(tmem + kC2TmUO + 64 * st,
+                            sdesc_sw128(a_st + kC2StQW + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
+                            sdesc_sw128(a_sb + s * 2048, 16384, 1024), idesc_uo, 1u);
+          umma_commit_elect(bars + kC2BarUO + st);
         }
+        ok = ok && warp_wait(kC2BarKReady + st, (c >> 1) & 1, kStatusTmaTimeout);
       }
       if (quad >= 2) {   // v_new rows -> decayed v_new tile
         ok = ok && warp_wait(kC2BarUO + st, (c >> 1) & 1, kStatusMmaTimeout);
@@ -640,30 +643,24 @@ __global__ void __launch_bounds__(kC2Threads, 1)
       }
       tc_fence_before();
       state_sync(1);
-      if (warp == 0) {   // M3, once K is in; the record part of the stage is free
-        if (ok && elect_one()) mbar_arrive(bars + kC2BarFreeA + st);
-        __syncwarp();
-        ok = ok && warp_wait(kC2BarKReady + st, (c >> 1) & 1, kStatusTmaTimeout);
-        if (ok) {
-          tc_fence_after();
-          if (elect_one()) {
+      const float decay = __expf(gam_last);
+      if (warp == 0 && ok) {   // M3; the record part of the stage is then free
+        tc_fence_after();
 #pragma unroll
-            for (int s = 0; s < 4; ++s)
-              umma_bf16(tmem + kC2TmS4, sdesc_sw128(a_st + kC2StK + s * 2048, 8192, 1024),
-                        sdesc_sw128(a_vnd + s * 2048, 8192, 1024), idesc_s, s > 0 ? 1u : 0u);
-            umma_commit(bars + kC2BarS);
-          }
-          __syncwarp();
-        }
+        for (int s = 0; s < 4; ++s)
+          umma_bf16_elect(tmem + kC2TmS4, sdesc_sw128(a_st + kC2StK + s * 2048, 8192, 1024),
+                          sdesc_sw128(a_vnd + s * 2048, 8192, 1024), idesc_s, s > 0 ? 1u : 0u);
+        umma_commit_elect(bars + kC2BarS);
+        if (elect_one()) mbar_arrive(bars + kC2BarFreeA + st);
+        __syncwarp();
+      }
+      if (c + 1 < nch) {
+        gammas(c + 1);
+        if (warp == 0) ok = ok && warp_wait(kC2BarM1 + (st ^ 1), ((c + 1) >> 1) & 1, kStatusMmaTimeout);
       }
       ok = ok && warp_wait(kC2BarS, c & 1, kStatusMmaTimeout);
       if (ok) {   // S_s^T = e^{gamma_last} S_s^T + D_S4
-        if (warp == 0) {
-          if (elect_one()) mbar_arrive(bars + kC2BarFreeB + st);
-          __syncwarp();
-        }
         tc_fence_after();
-        const float decay = __expf(gam_last);
         float r[32];
         tmem_ld32(tmem + kC2TmS4 + tm_lane + 32 * half, r);
         tmem_wait_ld();
@@ -671,6 +668,10 @@ __global__ void __launch_bounds__(kC2Threads, 1)
         for (int j = 0; j < 32; ++j) sreg[j] = fmaf(decay, sreg[j], r[j]);
         st_half_row_bf16(smem + kC2OffSB, row, 4 * half, sreg, 1.0f);
         fence_proxy_async_smem();
+        if (warp == 0) {
+          if (elect_one()) mbar_arrive(bars + kC2BarFreeB + st);
+          __syncwarp();
+        }
       }
       tc_fence_before();
       state_sync(2);

@@ -12,6 +12,11 @@ destination-passing style (all inputs, then the pre-allocated outputs):
 tensors), validate them like the TVM-FFI exports of this package do (raising
 ``ValueError``), and call the C ABI of ``libgdn_b200.so`` on the current torch
 stream.  ``decode`` / ``prefill`` are allocating conveniences on top.
+
+``gdn_decode_pool`` / ``gdn_mtp`` / ``mtp`` are the serving-side forms of the
+decode step that the next definitions of the same family add: a state pool
+addressed by per-sequence indices (fp32 or bf16 state), and T > 1 tokens per
+sequence with optional per-token intermediate states.
 ``load_tvm_kernel`` returns the TVM-FFI ``kernel`` itself, which is what the
 reference's harness binds.
 
@@ -85,6 +90,95 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state) -
     _lib.check(lib.gdn_b200_decode(
         _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
         float(scale or 0.0), _ptr(output), _ptr(new_state), B, h_qk, h_v, D, _stream(dev)))
+
+
+def gdn_decode_pool(q, k, v, state_pool, state_indices, A_log, a, dt_bias, b, scale, output,
+                    *, new_state_pool=None, output_state_indices=None,
+                    intermediate_states=None) -> None:
+    """Decode of T >= 1 tokens per sequence against a state pool (serving form).
+
+    Semantics of FlashInfer's pooled decode (``gated_delta_rule_decode_pretranspose``
+    with ``initial_state`` / ``initial_state_indices`` / ``output_state_indices``,
+    site flashinfer/gdn_decode.py:117-200) and, for T > 1, of the MTP definition
+    (site flashinfer/trace/templates/gdn.py:378-466), with q and k as given (no
+    L2 normalisation inside; the reference decode has none either).
+
+    q, k: [B, T, H_qk, 128] bf16; v: [B, T, H_v, 128] bf16; a, b: [B, T, H_v] bf16;
+    state_pool: [P, H_v, 128, 128] fp32 or bf16; state_indices: [B] int32/int64
+    (entry b reads slot state_indices[b]; negative = padding: zero output, no state
+    read or written); output: [B, T, H_v, 128] bf16.
+    new_state_pool: where final states go (default: state_pool itself, in place);
+    output_state_indices: [B] write slots (default: the read slots);
+    intermediate_states: [P, T, H_v, 128, 128] of the pool's dtype or None; the
+    state after token t of entry b lands at [state_indices[b], t].
+    """
+    dev = _cuda_device(q)
+    _require(q.dim() == 4 and v.dim() == 4, "q and v must be [B, T, H, D]")
+    B, T, h_qk, D = q.shape
+    h_v = v.shape[2]
+    _require(T >= 1, "T must be >= 1")
+    _require(isinstance(state_pool, torch.Tensor) and state_pool.dim() == 4,
+             "state_pool must be [P, H_v, D, D]")
+    sdt = state_pool.dtype
+    _require(sdt in (torch.float32, torch.bfloat16), "state_pool must be fp32 or bf16")
+    P = state_pool.shape[0]
+    _check(q, "q", torch.bfloat16, (B, T, h_qk, D), dev)
+    _check(k, "k", torch.bfloat16, (B, T, h_qk, D), dev)
+    _check(v, "v", torch.bfloat16, (B, T, h_v, D), dev)
+    _check(A_log, "A_log", torch.float32, (h_v,), dev)
+    _check(a, "a", torch.bfloat16, (B, T, h_v), dev)
+    _check(dt_bias, "dt_bias", torch.float32, (h_v,), dev)
+    _check(b, "b", torch.bfloat16, (B, T, h_v), dev)
+    _check(output, "output", torch.bfloat16, (B, T, h_v, D), dev)
+    _check(state_pool, "state_pool", sdt, (P, h_v, D, D), dev)
+    if new_state_pool is None:
+        new_state_pool = state_pool
+    _check(new_state_pool, "new_state_pool", sdt, (P, h_v, D, D), dev)
+    _require(isinstance(state_indices, torch.Tensor)
+             and state_indices.dtype in (torch.int32, torch.int64),
+             "state_indices must be an int32 or int64 tensor")
+    _check(state_indices, "state_indices", state_indices.dtype, (B,), dev)
+    if output_state_indices is not None:
+        _check(output_state_indices, "output_state_indices", state_indices.dtype, (B,), dev)
+    if intermediate_states is not None:
+        _check(intermediate_states, "intermediate_states", sdt, (P, T, h_v, D, D), dev)
+    lib = _lib.load()
+    _lib.check(lib.gdn_b200_decode_pool(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(state_pool), _ptr(new_state_pool),
+        1 if sdt == torch.bfloat16 else 0, _ptr(state_indices), _ptr(output_state_indices),
+        1 if state_indices.dtype == torch.int64 else 0, _ptr(intermediate_states),
+        _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b), float(scale or 0.0), _ptr(output),
+        B, T, P, h_qk, h_v, D, _stream(dev)))
+
+
+def gdn_mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
+            output, final_state, intermediate_states_buffer=None) -> None:
+    """Multi-token (MTP / speculative verify) decode in destination-passing style,
+    argument order of the MTP definition (site flashinfer/trace/templates/gdn.py:
+    378-466) with its outputs (output, final_state) appended.
+
+    ``final_state`` may be ``initial_state`` (in place, the serving case);
+    otherwise only the indexed slots of ``final_state`` are written, so a caller
+    wanting the definition's full returned pool copies ``initial_state`` into it
+    first (``mtp`` below does).
+    """
+    gdn_decode_pool(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
+                    output, new_state_pool=final_state,
+                    intermediate_states=intermediate_states_buffer)
+
+
+def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale=0.0,
+        intermediate_states_buffer=None):
+    """Allocating MTP decode with the definition's return values: ``(output,
+    final_state)``, ``final_state`` a new pool equal to ``initial_state`` except
+    at the indexed slots."""
+    B, T, _, D = q.shape
+    h_v = v.shape[2]
+    output = torch.empty((B, T, h_v, D), dtype=torch.bfloat16, device=q.device)
+    final_state = initial_state.clone()
+    gdn_mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale, output,
+            final_state, intermediate_states_buffer)
+    return output, final_state
 
 
 PREFILL_PATHS = ("split", "fused")

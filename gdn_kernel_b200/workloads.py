@@ -117,6 +117,42 @@ def make_decode_run(batch: int, steps: int, seed: int = 0, device="cpu", h_qk: i
     return first, tokens
 
 
+@dataclasses.dataclass
+class PoolDecodeInputs:
+    q: torch.Tensor          # [B, T, H_qk, D] bf16
+    k: torch.Tensor          # [B, T, H_qk, D] bf16
+    v: torch.Tensor          # [B, T, H_v, D] bf16
+    pool: torch.Tensor       # [P, H_v, D, D] fp32 or bf16
+    indices: torch.Tensor    # [B] int32 / int64: each entry's pool slot
+    A_log: torch.Tensor
+    a: torch.Tensor          # [B, T, H_v] bf16
+    dt_bias: torch.Tensor
+    b: torch.Tensor          # [B, T, H_v] bf16
+    scale: float
+
+
+def make_pool_decode_inputs(batch: int, seq_len: int, pool_size: int, seed: int = 0,
+                            device="cpu", h_qk: int = NUM_QK_HEADS, h_v: int = NUM_V_HEADS,
+                            d: int = HEAD_DIM, state_dtype=torch.float32,
+                            idx_dtype=torch.int32, state_std: float = 0.02) -> PoolDecodeInputs:
+    """Inputs of a pooled decode / MTP step: ``seq_len`` tokens per sequence, a
+    state pool of ``pool_size`` slots and a random slot permutation (entries
+    read distinct slots; ``pool_size >= batch``)."""
+    if pool_size < batch:
+        raise ValueError("pool_size must be >= batch")
+    gen = _gen(seed, device)
+    q = _unit_heads(_normal((batch, seq_len, h_qk, d), gen, device))
+    k = _unit_heads(_normal((batch, seq_len, h_qk, d), gen, device))
+    v = _normal((batch, seq_len, h_v, d), gen, device).to(torch.bfloat16)
+    A_log, dt_bias = _head_params(gen, device, h_v)
+    a = _normal((batch, seq_len, h_v), gen, device).to(torch.bfloat16)
+    b = _normal((batch, seq_len, h_v), gen, device).to(torch.bfloat16)
+    pool = _normal((pool_size, h_v, d, d), gen, device, std=state_std).to(state_dtype)
+    perm = torch.randperm(pool_size, generator=gen, device=device)[:batch]
+    return PoolDecodeInputs(q, k, v, pool, perm.to(idx_dtype), A_log, a, dt_bias, b,
+                            1.0 / math.sqrt(d))
+
+
 def varlen_lengths(num_seqs: int, lo: int, hi: int, seed: int) -> list:
     """Sequence lengths drawn uniformly from [lo, hi] by seed."""
     gen = torch.Generator().manual_seed(seed)

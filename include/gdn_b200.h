@@ -41,6 +41,7 @@ extern "C" {
 #define GDN_B200_STATUS_TMA_TIMEOUT 1u   /* a prefill TMA wait exceeded its bound */
 #define GDN_B200_STATUS_MMA_TIMEOUT 2u   /* a prefill tensor-core wait exceeded its bound */
 #define GDN_B200_STATUS_BAD_SEQLENS 4u   /* a cu_seqlens entry was outside [0, total_tokens] */
+#define GDN_B200_STATUS_BAD_INDEX 8u     /* a state-pool index was >= pool_size */
 
 /*
  * One T=1 decode step for `batch` sequences.
@@ -53,6 +54,40 @@ int gdn_b200_decode(const void* q, const void* k, const void* v, const float* st
                     double scale, void* output, float* new_state,
                     int64_t batch, int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
                     void* stream);
+
+/*
+ * Decode of `seq_len` >= 1 tokens per sequence against a state pool: the
+ * serving-side forms of the step above.  No counterpart in the reference's
+ * contest kit; the semantics are those of the next definitions of the same
+ * family: FlashInfer's pooled decode
+ * (gated_delta_rule_decode_pretranspose with initial_state, initial_state_indices,
+ * output_state_indices; site flashinfer/gdn_decode.py:117-200) and the MTP /
+ * speculative-verify definition (site flashinfer/trace/templates/gdn.py:378-466).
+ *
+ *   q, k [B,T,H_qk,D] bf16;  v [B,T,H_v,D] bf16;  a, b [B,T,H_v] bf16;
+ *   output [B,T,H_v,D] bf16;
+ *   state_pool, new_state_pool [P,H_v,D(v),D(k)], fp32 (state_is_bf16 = 0) or bf16 (= 1);
+ *     new_state_pool may alias state_pool (in-place, the serving case); only the slots
+ *     named by the indices are written;
+ *   read_indices, write_indices [B] int32 (indices_are_int64 = 0) or int64 (= 1):
+ *     entry b reads slot read_indices[b] and writes its final state to slot
+ *     write_indices[b] (write_indices = NULL: the read slot);
+ *   intermediate_states: NULL, or [P,T,H_v,D,D] of the state type; the state after
+ *     token t of entry b is stored at [read_indices[b], t] (for rollback).
+ * A negative index marks a padding entry: its outputs are zero and no state is read or
+ * written.  An index >= pool_size is treated as padding and sets
+ * GDN_B200_STATUS_BAD_INDEX.  Entries must not share a write slot, and no entry may
+ * write a slot another entry reads.  The recurrence runs in fp32; a bf16 pool is
+ * rounded once per stored state.
+ */
+int gdn_b200_decode_pool(const void* q, const void* k, const void* v,
+                         const void* state_pool, void* new_state_pool, int32_t state_is_bf16,
+                         const void* read_indices, const void* write_indices,
+                         int32_t indices_are_int64, void* intermediate_states,
+                         const float* A_log, const void* a, const float* dt_bias, const void* b,
+                         double scale, void* output, int64_t batch, int64_t seq_len,
+                         int64_t pool_size, int32_t num_qk_heads, int32_t num_v_heads,
+                         int32_t head_dim, void* stream);
 
 /*
  * Chunked (C=64) prefill over `num_seqs` packed variable-length sequences.

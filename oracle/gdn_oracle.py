@@ -194,3 +194,54 @@ def prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None
         return res + (chunk_states,)
     return res
 
+
+
+def decode_pool(q, k, v, pool, read_idx, A_log, a, dt_bias, b, scale=None, write_idx=None,
+                inter=None):
+    """Decode of T >= 1 tokens per sequence against a state pool.
+
+    Restates the MTP / speculative-verify definition (site
+    flashinfer/trace/templates/gdn.py:378-466, ``_gdn_mtp_reference``: per token
+    the decode step of ref kernel.cu:55-96, the state carried across the T
+    tokens in fp32, the state after token t stored at ``inter[read_idx[b], t]``)
+    and the pool addressing of FlashInfer's pooled decode (site
+    flashinfer/gdn_decode.py:117-200: entry b reads slot ``read_idx[b]`` and
+    writes slot ``write_idx[b]``, default the read slot; a negative index marks
+    padding, whose outputs are zero and whose state is neither read nor
+    written, the fp32 behaviour described at gdn_decode.py:182-195).
+
+    q, k: [B, T, H_qk, K] bf16; v: [B, T, H_v, V] bf16; a, b: [B, T, H_v];
+    pool: [P, H_v, V, K] fp32 or bf16; read_idx / write_idx: [B] integer;
+    inter: None or [P, T, H_v, V, K] of the pool's dtype (updated in place).
+    Returns (output [B, T, H_v, V] bf16, new_pool): ``new_pool`` is a copy of
+    ``pool`` with the written slots replaced; a bf16 pool is rounded once per
+    stored state.
+    """
+    B, T, h_qk, K = q.shape
+    h_v = v.shape[2]
+    scale = default_scale(scale, K)
+    rep = h_v // h_qk
+    log_g, beta = log_gate_beta(A_log, a, dt_bias, b)                  # [B, T, H_v]
+    g = torch.exp(log_g)
+    qf = q.float().repeat_interleave(rep, dim=2)                       # [B, T, H_v, K]
+    kf = k.float().repeat_interleave(rep, dim=2)
+    vf = v.float()
+    out = torch.zeros(B, T, h_v, v.shape[3], dtype=torch.float32)
+    new_pool = pool.clone()
+    P = pool.shape[0]
+    for bi in range(B):
+        r = int(read_idx[bi])
+        w = int(write_idx[bi]) if write_idx is not None else r
+        if r < 0 or w < 0 or r >= P or w >= P:
+            continue
+        S = pool[r].float()                                            # [H_v, V, K]
+        for t in range(T):
+            S = g[bi, t][:, None, None] * S
+            old_v = torch.matmul(S, kf[bi, t][..., None])[..., 0]      # [H_v, V]
+            delta = beta[bi, t][:, None] * (vf[bi, t] - old_v)
+            S = S + delta[..., None] * kf[bi, t][:, None, :]
+            out[bi, t] = scale * torch.matmul(S, qf[bi, t][..., None])[..., 0]
+            if inter is not None:
+                inter[r, t] = S.to(inter.dtype)
+        new_pool[w] = S.to(pool.dtype)
+    return out.to(torch.bfloat16), new_pool

@@ -123,7 +123,39 @@ def main():
     rec.update(state_summary(ns))
     np.savez_compressed(os.path.join(OUT, "prefill_qk16v32_T150.npz"), **rec)
     print("fixtures written to", OUT)
+    make_mtp()
+
+
+def make_mtp():
+    """Multi-token (MTP / speculative verify) decode against a state pool, from the
+    next definition of the same family: ``_gdn_mtp_reference`` in
+    ``flashinfer.trace.templates.gdn`` (flashinfer 0.6.11.post2).  B=3 sequences of
+    T=3 tokens, qk1_v2, a pool of 5 fp32 slots of which slots 2, 0 and 3 are read
+    (slots 1 and 4 stay untouched), and an intermediate-state buffer.  Inputs are
+    regenerated from the seed and checked against stored checksums; outputs are
+    stored in full, pool and intermediate states as row sums / sums of squares and
+    one complete head."""
+    from flashinfer.trace.templates.gdn import _gdn_mtp_reference
+
+    x = W.make_pool_decode_inputs(3, 3, 5, seed=21, h_qk=1, h_v=2)
+    idx = torch.tensor([2, 0, 3], dtype=torch.int32)
+    inter = torch.zeros(5, 3, 2, 128, 128, dtype=torch.float32)
+    o, final = _gdn_mtp_reference(x.q, x.k, x.v, x.pool, idx, x.A_log, x.a, x.dt_bias, x.b,
+                                  0.0, intermediate_states_buffer=inter)
+    rec = {"output": _np(o), "indices": idx.numpy()}
+    for n in ("q", "k", "v", "pool", "A_log", "a", "dt_bias", "b"):
+        rec[f"in_{n}"] = checksum(getattr(x, n).float())
+    rec["pool_rowsum"] = final.double().sum(-1).numpy()
+    rec["pool_rowsq"] = (final.double() ** 2).sum(-1).numpy()
+    rec["pool_slot2_head1"] = final[2, 1].numpy().copy()
+    rec["inter_rowsum"] = inter.double().sum(-1).numpy()
+    rec["inter_slot0_t1_head0"] = inter[0, 1, 0].numpy().copy()
+    np.savez_compressed(os.path.join(OUT, "mtp_b3_t3_qk1v2_pool5.npz"), **rec)
+    print("MTP fixture written to", OUT)
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["--mtp"]:
+        make_mtp()
+    else:
+        main()

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for name in _declared():
         assert hasattr(lib, name), name
     assert set(_declared()) == set(_lib._SIGNATURES), "ctypes table out of sync with the header"
-    assert lib.gdn_b200_abi_version() == 100
+    assert lib.gdn_b200_abi_version() == 101
 
 
 def _decode_call(lib, **kw):
@@ -92,3 +92,20 @@ def test_python_api_rejects_cpu_tensors():
     q = torch.zeros(1, 1, 16, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         K.gdn_decode(q, q, q, None, None, None, None, None, 0.0, None, None)
+
+
+def test_decode_pool_rejects_bad_arguments():
+    lib = _lib.load()
+    z = ctypes.c_void_p(0)
+
+    def call(batch=2, seq_len=3, pool=4, h_qk=16, h_v=32, d=128):
+        return lib.gdn_b200_decode_pool(z, z, z, z, z, 0, z, z, 0, z, z, z, z, z, 0.0, z,
+                                        batch, seq_len, pool, h_qk, h_v, d, z)
+
+    assert call(d=64) == _lib.GDN_B200_ERR_INVALID_ARGUMENT
+    assert call(seq_len=0) == _lib.GDN_B200_ERR_INVALID_ARGUMENT
+    assert b"seq_len" in lib.gdn_b200_last_error()
+    assert call(pool=0) == _lib.GDN_B200_ERR_INVALID_ARGUMENT
+    assert call() == _lib.GDN_B200_ERR_INVALID_ARGUMENT            # null pointers
+    assert b"null" in lib.gdn_b200_last_error()
+    assert call(batch=0) == _lib.GDN_B200_OK                         # nothing to do

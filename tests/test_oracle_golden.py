@@ -119,3 +119,47 @@ def test_chunked_matches_sequential_ragged():
                                x.cu_seqlens, x.scale)
     torch.testing.assert_close(o1.float(), o2.float(), atol=1e-2, rtol=1e-2)
     torch.testing.assert_close(s1, s2, atol=1e-5, rtol=1e-4)
+
+
+def _mtp_fixture_inputs(g):
+    x = W.make_pool_decode_inputs(3, 3, 5, seed=21, h_qk=1, h_v=2)
+    for n in ("q", "k", "v", "pool", "A_log", "a", "dt_bias", "b"):
+        np.testing.assert_allclose(_checksum(getattr(x, n).float()), g[f"in_{n}"], rtol=1e-12)
+    return x, torch.from_numpy(g["indices"].copy())
+
+
+def test_mtp_pool_matches_definition():
+    """Multi-token decode against a state pool, with intermediate states: the
+    oracle against the MTP definition function's fixture."""
+    g = _load("mtp_b3_t3_qk1v2_pool5.npz")
+    x, idx = _mtp_fixture_inputs(g)
+    inter = torch.zeros(5, 3, 2, 128, 128)
+    out, pool = O.decode_pool(x.q, x.k, x.v, x.pool, idx, x.A_log, x.a, x.dt_bias, x.b, 0.0,
+                              inter=inter)
+    ref = _t(g["output"]).float()
+    assert (out.float() - ref).abs().max().item() < 4e-3
+    np.testing.assert_allclose(pool.double().sum(-1).numpy(), g["pool_rowsum"], atol=1e-4)
+    np.testing.assert_allclose((pool.double() ** 2).sum(-1).numpy(), g["pool_rowsq"],
+                               rtol=1e-4, atol=1e-7)
+    np.testing.assert_allclose(pool[2, 1].numpy(), g["pool_slot2_head1"], atol=1e-5)
+    np.testing.assert_allclose(inter.double().sum(-1).numpy(), g["inter_rowsum"], atol=1e-4)
+    np.testing.assert_allclose(inter[0, 1, 0].numpy(), g["inter_slot0_t1_head0"], atol=1e-5)
+    # untouched slots are copied through
+    assert torch.equal(pool[1], x.pool[1]) and torch.equal(pool[4], x.pool[4])
+
+
+def test_pool_decode_padding_and_write_slots():
+    """Host semantics of the pool addressing: a negative index is padding (zero
+    output, no state traffic); write slots may differ from read slots; T=1 with
+    identity slots is the plain decode step."""
+    x = W.make_pool_decode_inputs(3, 1, 6, seed=4, h_qk=1, h_v=2)
+    read = torch.tensor([4, -1, 0])
+    write = torch.tensor([1, 3, 5])
+    out, pool = O.decode_pool(x.q, x.k, x.v, x.pool, read, x.A_log, x.a, x.dt_bias, x.b, 0.0,
+                              write_idx=write)
+    assert out[1].abs().max().item() == 0.0
+    for s in (0, 2, 3, 4):      # not written (3 belongs to the padding entry)
+        assert torch.equal(pool[s], x.pool[s])
+    o1, s1 = O.decode_step(x.q[[0]], x.k[[0]], x.v[[0]], x.pool[[4]], x.A_log, x.a[[0]],
+                           x.dt_bias, x.b[[0]], 0.0)
+    assert torch.equal(out[[0]], o1) and torch.equal(pool[1], s1[0])
