@@ -10,6 +10,8 @@ Also reported on the same line:
 * ``prefill``: configs[2] (one 8192-token sequence, chunked C=64) tokens/s and
   its tensor/HBM roofline, plus configs[3] (16 packed sequences) tokens/s;
 * ``decode_sweep``: configs[1] B in {1, 8, 32, 64, 128, 256};
+* ``decode_pool``: the pooled / multi-token decode at B=64 (fp32 and bf16 state
+  pools, T=1 and T=4, with and without per-token intermediate states);
 * ``roofline``: the decode kernel against the measured HBM copy bandwidth;
 * ``cpu_baseline``: the fp32 CPU oracle on the host cores (bounded sample);
 * ``e2e``: the decode metric through the C ABI with pinned host buffers,
@@ -180,6 +182,31 @@ def time_decode(K, batch, steps, warmup, flush, seed=0):
     times = [e0.elapsed_time(e1) for e0, e1 in ev]
     del x, out
     return times
+
+
+def time_decode_pool(K, batch, seq_len, steps, warmup, flush, state_dtype, inter, seed=0):
+    """Per-call device time (ms) of the pooled / multi-token decode, in place on a
+    pool of 2*batch slots (entries read distinct random slots)."""
+    from gdn_kernel_b200 import workloads as W
+
+    x = W.make_pool_decode_inputs(batch, seq_len, 2 * batch, seed=seed, device="cuda",
+                                  state_dtype=state_dtype)
+    out = torch.empty(batch, seq_len, H_V, D, dtype=torch.bfloat16, device="cuda")
+    ibuf = (torch.empty(2 * batch, seq_len, H_V, D, D, dtype=state_dtype, device="cuda")
+            if inter else None)
+    args = (x.q, x.k, x.v, x.pool, x.indices, x.A_log, x.a, x.dt_bias, x.b, x.scale, out)
+    for _ in range(warmup):
+        flush.zero_()
+        K.gdn_decode_pool(*args, intermediate_states=ibuf)
+    torch.cuda.synchronize()
+    ev = [_events() for _ in range(steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        K.gdn_decode_pool(*args, intermediate_states=ibuf)
+        e1.record()
+    torch.cuda.synchronize()
+    return [e0.elapsed_time(e1) for e0, e1 in ev]
 
 
 def time_decode_e2e(K, batch, steps, warmup, flush, seed=0):
@@ -368,6 +395,22 @@ def run_gpu(args, rank, world, local_rank):
                              "frac_hbm": round(b * STATE_BYTES_PER_SEQ / (ms * 1e-3) / 1e9
                                                / hbm_peak, 3)}
         extra["decode_sweep"] = sweep
+        # ---- pooled / multi-token decode (the serving forms of the step)
+        pool = {}
+        for name, seq_len, sdt, inter in (("B64_T1_fp32", 1, torch.float32, False),
+                                          ("B64_T1_bf16", 1, torch.bfloat16, False),
+                                          ("B64_T4_fp32", 4, torch.float32, False),
+                                          ("B64_T4_fp32_intermediate", 4, torch.float32, True)):
+            ts = time_decode_pool(K, 64, seq_len, 30, 3, flush, sdt, inter, seed=7000)
+            ms = statistics.median(ts)
+            esz = 4 if sdt == torch.float32 else 2
+            # state read once and written once, plus one stored state per token
+            nbytes = 64 * H_V * D * D * esz * (2 + (seq_len if inter else 0))
+            pool[name] = {"us": round(ms * 1e3, 2),
+                          "tokens_per_s": round(64 * seq_len / (ms * 1e-3), 1),
+                          "state_GBps": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                          "frac_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3)}
+        extra["decode_pool"] = pool
         # ---- prefill configs[2] and configs[3]
         from gdn_kernel_b200 import workloads as W
         pre = {}
