@@ -1,19 +1,38 @@
-// GDN decode (T = 1): one fused, bandwidth-bound pass over the fp32 k-last
-// state [B, H_v, V, K].
+// GDN decode: one fused, bandwidth-bound pass over the k-last state
+// [*, H_v, V, K] per call, for T >= 1 tokens per sequence.
 //
-// Semantics follow the reference decode kernel (ref solution/cuda/kernel.cu:21-97):
+// Per token the step is the reference decode step (ref solution/cuda/kernel.cu:21-97):
 //   g = exp(-exp(A_log) softplus(a + dt_bias)),  beta = sigmoid(b)
 //   S <- g S;  delta = beta (v - S k);  S += delta k^T;  o = scale S q
 // written per state row v (rows are independent in the k-last layout):
 //   s = g S_v;  delta_v = beta (v_v - <s,k>);  S_v' = s + delta_v k;
 //   o_v = scale (<s,q> + delta_v <k,q>)
 //
-// Layout on the SM: a CTA of 4 warps covers kRowsPerCta = 16 * kIters rows of
-// one (batch, v-head) state.  Eight lanes share one 512-byte state row (each
-// lane holds four float4 at columns 4*l8 + 32*j), so one warp instruction moves
-// four full rows, fully coalesced, and the two row reductions are 3-level xor
-// shuffles.  Each warp streams 4 * kIters rows through a register pipeline
-// kPipe iterations deep, writing every row back in place.
+// One kernel serves the reference's decode entry point and its serving forms:
+//   * the reference decode (gdn_b200_decode): T = 1, state [B, H_v, V, K] fp32
+//     indexed by the batch entry, state == nullptr meaning a zero state
+//     (ref kernel.cu:135-139), new_state possibly aliasing state;
+//   * a state pool [P, H_v, V, K] (fp32 or bf16): entry b reads slot
+//     read_idx[b] and writes slot write_idx[b] (= read_idx[b] when no write
+//     indices are given), as FlashInfer's pooled decode
+//     (site flashinfer/gdn_decode.py:117-200);
+//   * T > 1 tokens per sequence (multi-token prediction / speculative verify):
+//     the T tokens run in order on the state held in registers, each token's
+//     output is written, and optionally the state after every token is kept in
+//     intermediate[read_idx[b], t] (site flashinfer/trace/templates/gdn.py:
+//     378-466, _gdn_mtp_reference).
+// The recurrence runs in fp32 registers; a bf16 pool is rounded once per stored
+// state.  A negative index marks a padding entry: its outputs are written as zero
+// and no state is read or written (the fp32 behaviour of site
+// flashinfer/gdn_decode.py:182-195).  An index >= pool_size is treated the same
+// way and raises kStatusBadIndex.
+//
+// Layout on the SM: a CTA of 4 warps; eight lanes share one state row, each
+// lane owning 16 columns read as 16-byte vectors, so one warp instruction moves
+// four rows fully coalesced and the row reductions are 3-level xor shuffles.
+// Each thread carries kRowIters rows (two 512-byte fp32 rows, or four 256-byte
+// bf16 rows) whose loads are all issued before any use, keeping 16 KiB (fp32)
+// or 16 KiB (bf16) of state in flight per CTA.
 #pragma once
 
 #include "gdn_ptx.cuh"
@@ -22,52 +41,18 @@ namespace gdn {
 
 constexpr int kHeadDim = 128;
 constexpr int kDecodeThreads = 128;
-#ifndef GDN_DECODE_ITERS
-#define GDN_DECODE_ITERS 1   // 4 rows per warp per iteration
-#endif
-#ifndef GDN_DECODE_PIPE
-#define GDN_DECODE_PIPE 1    // iterations of loads in flight ahead of the reduction
-#endif
-#ifndef GDN_DECODE_LDHINT
-#define GDN_DECODE_LDHINT 1  // L1::no_allocate + L2::256B prefetch on state loads
-#endif
-constexpr int kDecodeIters = GDN_DECODE_ITERS;
-constexpr int kDecodePipe = GDN_DECODE_PIPE;
-constexpr int kDecodeRowsPerCta = 16 * kDecodeIters;
-constexpr int kDecodeCtasPerHead = kHeadDim / kDecodeRowsPerCta;
-static_assert(kHeadDim % kDecodeRowsPerCta == 0, "rows per CTA must divide 128");
-
-struct DecodeParams {
-  const __nv_bfloat16* q;        // [B, 1, H_qk, K]
-  const __nv_bfloat16* k;        // [B, 1, H_qk, K]
-  const __nv_bfloat16* v;        // [B, 1, H_v, V]
-  const float* state;            // [B, H_v, V, K] or nullptr (zero state)
-  const float* A_log;            // [H_v]
-  const __nv_bfloat16* a;        // [B, 1, H_v]
-  const float* dt_bias;          // [H_v]
-  const __nv_bfloat16* b;        // [B, 1, H_v]
-  float scale;
-  __nv_bfloat16* out;            // [B, 1, H_v, V]
-  float* new_state;              // [B, H_v, V, K], may alias state
-  int h_qk;
-  int h_v;
-};
 
 __device__ __forceinline__ float softplus20(float x) {
   return x > 20.0f ? x : log1pf(expf(x));
 }
 
+// State loads bypass L1 (each byte is read once) and ask L2 for 256-byte
+// sectors, the row pair a warp instruction touches.
 __device__ __forceinline__ float4 ld_state(const float* p) {
   float4 r;
-#if GDN_DECODE_LDHINT
   asm volatile("ld.global.L1::no_allocate.L2::256B.v4.f32 {%0,%1,%2,%3}, [%4];"
                : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
                : "l"(p));
-#else
-  asm volatile("ld.global.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
-               : "l"(p));
-#endif
   return r;
 }
 
@@ -77,115 +62,325 @@ __device__ __forceinline__ void st_state(float* p, float4 r) {
                : "memory");
 }
 
-__device__ __forceinline__ void load_bf16x4(const __nv_bfloat16* p, float* dst) {
-  uint2 u = *reinterpret_cast<const uint2*>(p);
-  __nv_bfloat162 lo = *reinterpret_cast<__nv_bfloat162*>(&u.x);
-  __nv_bfloat162 hi = *reinterpret_cast<__nv_bfloat162*>(&u.y);
-  float2 f0 = __bfloat1622float2(lo), f1 = __bfloat1622float2(hi);
-  dst[0] = f0.x; dst[1] = f0.y; dst[2] = f1.x; dst[3] = f1.y;
+constexpr unsigned int kStatusBadIndex = 8u;   // a state index >= pool_size
+
+struct DecodeParams {
+  const __nv_bfloat16* q;        // [B, T, H_qk, K]
+  const __nv_bfloat16* k;        // [B, T, H_qk, K]
+  const __nv_bfloat16* v;        // [B, T, H_v, V]
+  const void* pool;              // [P, H_v, V, K] fp32 or bf16, or nullptr (zero state)
+  void* new_pool;                // [P, H_v, V, K], may alias pool
+  void* inter;                   // [P, T, H_v, V, K] or nullptr
+  const void* read_idx;          // [B] int32 / int64, or nullptr (slot = batch entry)
+  const void* write_idx;         // [B] int32 / int64, or nullptr (= read_idx)
+  int idx_is_int64;
+  const float* A_log;            // [H_v]
+  const __nv_bfloat16* a;        // [B, T, H_v]
+  const float* dt_bias;          // [H_v]
+  const __nv_bfloat16* b;        // [B, T, H_v]
+  float scale;
+  __nv_bfloat16* out;            // [B, T, H_v, V]
+  unsigned int* status;
+  long long pool_size;
+  int T;
+  int h_qk;
+  int h_v;
+};
+
+__device__ __forceinline__ long long pool_index(const void* idx, int is64, int b) {
+  return is64 ? reinterpret_cast<const long long*>(idx)[b]
+              : static_cast<long long>(reinterpret_cast<const int*>(idx)[b]);
 }
 
-template <bool kHasState>
+// Per state type: each lane owns 16 columns of a row, read as kAcc vector
+// accesses of kVec elements at columns kVec*l8 + 8*kVec*j + e (j < kAcc, e <
+// kVec), so every access is 16 bytes and 8 lanes cover a row.  A bf16 row is
+// half the bytes, so a bf16 thread carries twice the rows.
+template <typename StateT> struct DecodeLayout;
+template <> struct DecodeLayout<float> {
+  static constexpr int kVec = 4, kAcc = 4, kRowIters = 2;
+};
+template <> struct DecodeLayout<__nv_bfloat16> {
+  static constexpr int kVec = 8, kAcc = 2, kRowIters = 4;
+};
+
+__device__ __forceinline__ void ld_vec(const float* p, float* x) {
+  const float4 r = ld_state(p);
+  x[0] = r.x; x[1] = r.y; x[2] = r.z; x[3] = r.w;
+}
+__device__ __forceinline__ void ld_vec(const __nv_bfloat16* p, float* x) {
+  uint32_t w[4];
+  asm volatile("ld.global.L1::no_allocate.L2::256B.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+               : "l"(p));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[i]));
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void st_vec(float* p, const float* x) {
+  st_state(p, make_float4(x[0], x[1], x[2], x[3]));
+}
+__device__ __forceinline__ void st_vec(__nv_bfloat16* p, const float* x) {
+  asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(pack_bf16x2(x[0], x[1])),
+               "r"(pack_bf16x2(x[2], x[3])), "r"(pack_bf16x2(x[4], x[5])),
+               "r"(pack_bf16x2(x[6], x[7]))
+               : "memory");
+}
+
+// One token's inputs for this thread, kept as packed bf16 until used: the q/k
+// fragments (16 columns each), the gate inputs and this thread's v entries.
+template <int kRowIters>
+struct TokIn {
+  uint32_t q[8], k[8];
+  __nv_bfloat16 a, b, v[kRowIters];
+};
+
+// kVec consecutive bf16 (kVec / 2 words) from global memory.
+template <int kVec>
+__device__ __forceinline__ void ld_words(const __nv_bfloat16* p, uint32_t* w) {
+  if constexpr (kVec == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    w[0] = u.x; w[1] = u.y;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+  }
+}
+
+__device__ __forceinline__ void unpack16(const uint32_t* w, float* x) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+// Tokens whose inputs a CTA stages in shared memory at a time (T > 1).
+constexpr int kTokGroup = 16;
+
+// kHasState = false is the reference decode's null state (a zero initial state,
+// no state reads).  kMulti = false is the T = 1 instance: the token's inputs go
+// straight to registers.  kMulti = true stages the inputs of up to kTokGroup tokens in
+// shared memory with one round of loads, so the per-token steps do not each
+// wait out a global-memory latency.
+template <typename StateT, bool kMulti, bool kHasState>
 __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams p) {
-  constexpr int kIters = kDecodeIters;
-  constexpr int kPipe = kDecodePipe < kDecodeIters ? kDecodePipe : kDecodeIters;
-  constexpr int kBuf = kPipe < kDecodeIters ? kPipe + 1 : kDecodeIters;
-  const int bh = blockIdx.x / kDecodeCtasPerHead;   // batch * H_v + v-head
-  const int rblk = blockIdx.x % kDecodeCtasPerHead;
+  using L = DecodeLayout<StateT>;
+  constexpr int kVec = L::kVec, kAcc = L::kAcc, kRI = L::kRowIters;
+  constexpr int kRows = 16 * kRI;   // rows per CTA: 4 warps x 4 rows x kRowIters
+  constexpr int kCtasPerHead = kHeadDim / kRows;
+  const int bh = blockIdx.x / kCtasPerHead;   // batch * H_v + v-head
+  const int rblk = blockIdx.x % kCtasPerHead;
   const int h = bh % p.h_v;
   const int bidx = bh / p.h_v;
-  const int hq = h / (p.h_v / p.h_qk);       // GQA: v-head h reads qk-head h / (H_v/H_qk)
+  const int hq = h / (p.h_v / p.h_qk);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int sub = lane >> 3;                 // row inside the warp's 4-row group
-  const int l8 = lane & 7;                   // column slot inside the row
+  const int l8 = lane & 7;
+  const int row0 = rblk * kRows + warp * (4 * kRI) + (lane >> 3);   // rows row0 + 4 i
+  const size_t hd2 = static_cast<size_t>(kHeadDim) * kHeadDim;
 
-  // State loads first: they are independent of the gate and q/k loads and
-  // carry the DRAM latency that everything else overlaps with.
-  const size_t sbase = static_cast<size_t>(bh) * kHeadDim * kHeadDim;
-  // iteration it touches row row0 + 4*it
-  const int row0 = rblk * kDecodeRowsPerCta + warp * (4 * kIters) + sub;
-  const float* src = kHasState ? p.state + sbase + static_cast<size_t>(row0) * kHeadDim + 4 * l8
-                               : nullptr;
-  float* dst = p.new_state + sbase + static_cast<size_t>(row0) * kHeadDim + 4 * l8;
-  const __nv_bfloat16* vrow = p.v + static_cast<size_t>(bh) * kHeadDim;
-
-  float4 buf[kBuf][4];
-  if (kHasState) {
+  // Token inputs of token t (issued before they are needed: the slot index
+  // load, then token 0's inputs, then the state rows).
+  auto load_tok = [&](int t, TokIn<kRI>& in) {
+    const size_t tok = static_cast<size_t>(bidx) * p.T + t;
+    const size_t qk_off = (tok * p.h_qk + hq) * kHeadDim;
 #pragma unroll
-    for (int it = 0; it < kPipe; ++it)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) buf[it % kBuf][j] = ld_state(src + it * 4 * kHeadDim + 32 * j);
-  }
-
-  // Gate and beta for this (batch, v-head) (ref kernel.cu:44-53).
-  const float av = __bfloat162float(p.a[bh]);
-  const float bv = __bfloat162float(p.b[bh]);
-  const float g = expf(-expf(p.A_log[h]) * softplus20(av + p.dt_bias[h]));
-  const float beta = 1.0f / (1.0f + expf(-bv));
-
-  // q and k fragments for columns 4*l8 + 32*j + e.
-  const size_t qk_off = (static_cast<size_t>(bidx) * p.h_qk + hq) * kHeadDim;
-  float qf[16], kf[16];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    load_bf16x4(p.q + qk_off + 4 * l8 + 32 * j, qf + 4 * j);
-    load_bf16x4(p.k + qk_off + 4 * l8 + 32 * j, kf + 4 * j);
-  }
-  float qk = 0.f;
-#pragma unroll
-  for (int e = 0; e < 16; ++e) qk = fmaf(qf[e], kf[e], qk);
-  qk += __shfl_xor_sync(0xffffffffu, qk, 1);
-  qk += __shfl_xor_sync(0xffffffffu, qk, 2);
-  qk += __shfl_xor_sync(0xffffffffu, qk, 4);
-
-  float outv[kIters];
-#pragma unroll
-  for (int it = 0; it < kIters; ++it) {
-    if (kHasState && it + kPipe < kIters) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        buf[(it + kPipe) % kBuf][j] = ld_state(src + (it + kPipe) * 4 * kHeadDim + 32 * j);
+    for (int j = 0; j < kAcc; ++j) {
+      ld_words<kVec>(p.q + qk_off + kVec * l8 + 8 * kVec * j, in.q + (kVec / 2) * j);
+      ld_words<kVec>(p.k + qk_off + kVec * l8 + 8 * kVec * j, in.k + (kVec / 2) * j);
     }
-    float s[16];
+    in.a = p.a[tok * p.h_v + h];
+    in.b = p.b[tok * p.h_v + h];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (kHasState) {
-        const float4 x = buf[it % kBuf][j];
-        s[4 * j + 0] = g * x.x; s[4 * j + 1] = g * x.y;
-        s[4 * j + 2] = g * x.z; s[4 * j + 3] = g * x.w;
-      } else {
-        s[4 * j + 0] = s[4 * j + 1] = s[4 * j + 2] = s[4 * j + 3] = 0.f;
+    for (int i = 0; i < kRI; ++i) in.v[i] = p.v[(tok * p.h_v + h) * kHeadDim + row0 + 4 * i];
+  };
+
+  // Slots: the batch entry itself without indices (the reference decode).
+  long long ridx = p.read_idx ? pool_index(p.read_idx, p.idx_is_int64, bidx) : bidx;
+  long long widx = p.write_idx ? pool_index(p.write_idx, p.idx_is_int64, bidx) : ridx;
+  TokIn<kRI> cur;
+  if constexpr (!kMulti) load_tok(0, cur);
+  if (ridx >= p.pool_size || widx >= p.pool_size) {
+    if (threadIdx.x == 0 && rblk == 0) atomicOr(p.status, kStatusBadIndex);
+    ridx = -1;
+  }
+  if (ridx < 0 || widx < 0) {   // padding entry: zero outputs, no state traffic
+    if (l8 == 0)
+      for (int t = 0; t < p.T; ++t)
+#pragma unroll
+        for (int i = 0; i < kRI; ++i)
+          p.out[((static_cast<size_t>(bidx) * p.T + t) * p.h_v + h) * kHeadDim + row0 + 4 * i] =
+              __float2bfloat16(0.f);
+    return;
+  }
+
+  // This thread's state: rows row0 + 4 i, 16 columns each.
+  const StateT* src = static_cast<const StateT*>(p.pool) + (ridx * p.h_v + h) * hd2 +
+                      static_cast<size_t>(row0) * kHeadDim + kVec * l8;
+  float st[kRI][16];
+  if constexpr (kHasState) {
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
+#pragma unroll
+      for (int j = 0; j < kAcc; ++j)
+        ld_vec(src + 4 * i * kHeadDim + 8 * kVec * j, st[i] + kVec * j);
+  } else {   // no state: a zero initial state (ref kernel.cu:135-139)
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
+#pragma unroll
+      for (int e = 0; e < 16; ++e) st[i][e] = 0.f;
+  }
+
+  const float neg_exp_alog = -expf(p.A_log[h]);
+  const float dtb = p.dt_bias[h];
+  // One token step on this thread's rows (inputs already unpacked).
+  auto step = [&](int t, const float* qf, const float* kf, float av, float bv,
+                  const float* vv) {
+    const size_t tok = static_cast<size_t>(bidx) * p.T + t;
+    const float g = expf(neg_exp_alog * softplus20(av + dtb));
+    const float beta = 1.0f / (1.0f + expf(-bv));
+    float qk = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) qk = fmaf(qf[e], kf[e], qk);
+    qk += __shfl_xor_sync(0xffffffffu, qk, 1);
+    qk += __shfl_xor_sync(0xffffffffu, qk, 2);
+    qk += __shfl_xor_sync(0xffffffffu, qk, 4);
+#pragma unroll
+    for (int i = 0; i < kRI; ++i) {
+      float s[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) s[e] = g * st[i][e];
+      float dk = 0.f, dq = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        dk = fmaf(s[e], kf[e], dk);
+        dq = fmaf(s[e], qf[e], dq);
+      }
+#pragma unroll
+      for (int m = 1; m < 8; m <<= 1) {
+        dk += __shfl_xor_sync(0xffffffffu, dk, m);
+        dq += __shfl_xor_sync(0xffffffffu, dq, m);
+      }
+      const float delta = beta * (vv[i] - dk);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) st[i][e] = fmaf(delta, kf[e], s[e]);
+      if (l8 == 0)
+        p.out[(tok * p.h_v + h) * kHeadDim + row0 + 4 * i] =
+            __float2bfloat16(p.scale * (dq + delta * qk));
+    }
+    if (p.inter) {   // state after token t, at [read slot, t]
+      StateT* dst = static_cast<StateT*>(p.inter) + ((ridx * p.T + t) * p.h_v + h) * hd2 +
+                    static_cast<size_t>(row0) * kHeadDim + kVec * l8;
+#pragma unroll
+      for (int i = 0; i < kRI; ++i)
+#pragma unroll
+        for (int j = 0; j < kAcc; ++j)
+          st_vec(dst + 4 * i * kHeadDim + 8 * kVec * j, st[i] + kVec * j);
+    }
+  };
+
+  if constexpr (!kMulti) {
+    float qf[16], kf[16], vv[kRI];
+    unpack16(cur.q, qf);
+    unpack16(cur.k, kf);
+#pragma unroll
+    for (int i = 0; i < kRI; ++i) vv[i] = __bfloat162float(cur.v[i]);
+    step(0, qf, kf, __bfloat162float(cur.a), __bfloat162float(cur.b), vv);
+  } else {
+    // Staged token inputs: q and k rows (256 B each), a, b, and this CTA's v rows.
+    __shared__ __align__(16) __nv_bfloat16 sq[kTokGroup][kHeadDim];
+    __shared__ __align__(16) __nv_bfloat16 sk[kTokGroup][kHeadDim];
+    __shared__ float sa[kTokGroup], sb[kTokGroup];
+    __shared__ __nv_bfloat16 sv[kTokGroup][kRows];
+    const int tid = threadIdx.x;
+    for (int t0 = 0; t0 < p.T; t0 += kTokGroup) {
+      const int n = min(kTokGroup, p.T - t0);
+      __syncthreads();   // the previous group is consumed
+      for (int e = tid; e < n * 16; e += kDecodeThreads) {   // 16 x 16 B per row
+        const int tt = e >> 4, c = e & 15;
+        const size_t qk_off =
+            ((static_cast<size_t>(bidx) * p.T + t0 + tt) * p.h_qk + hq) * kHeadDim + 8 * c;
+        reinterpret_cast<uint4*>(&sq[tt][0])[c] = *reinterpret_cast<const uint4*>(p.q + qk_off);
+        reinterpret_cast<uint4*>(&sk[tt][0])[c] = *reinterpret_cast<const uint4*>(p.k + qk_off);
+      }
+      for (int e = tid; e < n * kRows; e += kDecodeThreads) {
+        const int tt = e / kRows, r = e % kRows;
+        sv[tt][r] = p.v[((static_cast<size_t>(bidx) * p.T + t0 + tt) * p.h_v + h) * kHeadDim +
+                        rblk * kRows + r];
+      }
+      if (tid < n) {
+        const size_t gate_off = (static_cast<size_t>(bidx) * p.T + t0 + tid) * p.h_v + h;
+        sa[tid] = __bfloat162float(p.a[gate_off]);
+        sb[tid] = __bfloat162float(p.b[gate_off]);
+      }
+      __syncthreads();
+      for (int tt = 0; tt < n; ++tt) {
+        float qf[16], kf[16], vv[kRI];
+#pragma unroll
+        for (int j = 0; j < kAcc; ++j) {
+          uint32_t wq[kVec / 2], wk[kVec / 2];
+          if constexpr (kVec == 4) {
+            const uint2 uq = *reinterpret_cast<const uint2*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
+            const uint2 uk = *reinterpret_cast<const uint2*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
+            wq[0] = uq.x; wq[1] = uq.y; wk[0] = uk.x; wk[1] = uk.y;
+          } else {
+            const uint4 uq = *reinterpret_cast<const uint4*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
+            const uint4 uk = *reinterpret_cast<const uint4*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
+            wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
+            wk[0] = uk.x; wk[1] = uk.y; wk[2] = uk.z; wk[3] = uk.w;
+          }
+#pragma unroll
+          for (int w = 0; w < kVec / 2; ++w) {
+            const float2 fq = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wq[w]));
+            const float2 fk = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wk[w]));
+            qf[kVec * j + 2 * w] = fq.x; qf[kVec * j + 2 * w + 1] = fq.y;
+            kf[kVec * j + 2 * w] = fk.x; kf[kVec * j + 2 * w + 1] = fk.y;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kRI; ++i)
+          vv[i] = __bfloat162float(sv[tt][row0 - rblk * kRows + 4 * i]);
+        step(t0 + tt, qf, kf, sa[tt], sb[tt], vv);
       }
     }
-    float dk = 0.f, dq = 0.f;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      dk = fmaf(s[e], kf[e], dk);
-      dq = fmaf(s[e], qf[e], dq);
-    }
-#pragma unroll
-    for (int m = 1; m < 8; m <<= 1) {
-      dk += __shfl_xor_sync(0xffffffffu, dk, m);
-      dq += __shfl_xor_sync(0xffffffffu, dq, m);
-    }
-    const float vv = __bfloat162float(vrow[row0 + 4 * it]);
-    const float delta = beta * (vv - dk);
-    outv[it] = p.scale * (dq + delta * qk);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float4 y;
-      y.x = fmaf(delta, kf[4 * j + 0], s[4 * j + 0]);
-      y.y = fmaf(delta, kf[4 * j + 1], s[4 * j + 1]);
-      y.z = fmaf(delta, kf[4 * j + 2], s[4 * j + 2]);
-      y.w = fmaf(delta, kf[4 * j + 3], s[4 * j + 3]);
-      st_state(dst + it * 4 * kHeadDim + 32 * j, y);
-    }
   }
-  if (l8 == 0) {
-    __nv_bfloat16* orow = p.out + static_cast<size_t>(bh) * kHeadDim;
+  StateT* dst = static_cast<StateT*>(p.new_pool) + (widx * p.h_v + h) * hd2 +
+                static_cast<size_t>(row0) * kHeadDim + kVec * l8;
 #pragma unroll
-    for (int it = 0; it < kIters; ++it) orow[row0 + 4 * it] = __float2bfloat16(outv[it]);
+  for (int i = 0; i < kRI; ++i)
+#pragma unroll
+    for (int j = 0; j < kAcc; ++j) st_vec(dst + 4 * i * kHeadDim + 8 * kVec * j, st[i] + kVec * j);
+}
+
+// CTAs per (batch, v-head) of gdn_decode_kernel<StateT, *>.
+template <typename StateT>
+constexpr int decode_ctas_per_head() {
+  return kHeadDim / (16 * DecodeLayout<StateT>::kRowIters);
+}
+
+// Launch for `batch` entries; the instance follows the state type, T and
+// whether there is a state (multi-token and pooled calls always have one).
+inline void launch_decode(const DecodeParams& p, long long batch, bool state_bf16,
+                          cudaStream_t st) {
+  if (state_bf16) {
+    const dim3 grid(static_cast<unsigned>(batch * p.h_v * decode_ctas_per_head<__nv_bfloat16>()));
+    if (p.T > 1)
+      gdn_decode_kernel<__nv_bfloat16, true, true><<<grid, kDecodeThreads, 0, st>>>(p);
+    else
+      gdn_decode_kernel<__nv_bfloat16, false, true><<<grid, kDecodeThreads, 0, st>>>(p);
+  } else {
+    const dim3 grid(static_cast<unsigned>(batch * p.h_v * decode_ctas_per_head<float>()));
+    if (p.T > 1)
+      gdn_decode_kernel<float, true, true><<<grid, kDecodeThreads, 0, st>>>(p);
+    else if (p.pool)
+      gdn_decode_kernel<float, false, true><<<grid, kDecodeThreads, 0, st>>>(p);
+    else
+      gdn_decode_kernel<float, false, false><<<grid, kDecodeThreads, 0, st>>>(p);
   }
 }
 

@@ -12,7 +12,6 @@
 
 #include "gdn_b200.h"
 #include "decode_kernel.cuh"
-#include "decode_pool_kernel.cuh"
 #include "prefill_split.cuh"
 
 namespace gdn {
@@ -136,7 +135,7 @@ extern "C" int gdn_b200_decode(const void* q, const void* k, const void* v, cons
   t_last_error.clear();
   if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
   if (batch < 0) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch must be >= 0");
-  if (batch * num_v_heads * kDecodeCtasPerHead > 0x7fffffffLL)
+  if (batch * num_v_heads * decode_ctas_per_head<float>() > 0x7fffffffLL)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch * num_v_heads exceeds the grid limit");
   if (batch == 0) return GDN_B200_OK;
   if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !new_state)
@@ -151,22 +150,24 @@ extern "C" int gdn_b200_decode(const void* q, const void* k, const void* v, cons
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k);
   p.v = static_cast<const __nv_bfloat16*>(v);
-  p.state = state;
+  p.pool = state;              // slot = batch entry (no indices); nullptr = zero state
+  p.new_pool = new_state;
+  p.inter = nullptr;
+  p.read_idx = nullptr;
+  p.write_idx = nullptr;
+  p.idx_is_int64 = 0;
   p.A_log = A_log;
   p.a = static_cast<const __nv_bfloat16*>(a);
   p.dt_bias = dt_bias;
   p.b = static_cast<const __nv_bfloat16*>(b);
   p.scale = resolve_scale(scale);
   p.out = static_cast<__nv_bfloat16*>(output);
-  p.new_state = new_state;
+  p.status = status;
+  p.pool_size = batch;
+  p.T = 1;
   p.h_qk = num_qk_heads;
   p.h_v = num_v_heads;
-  const dim3 grid(static_cast<unsigned>(batch * num_v_heads * kDecodeCtasPerHead));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (state)
-    gdn_decode_kernel<true><<<grid, kDecodeThreads, 0, st>>>(p);
-  else
-    gdn_decode_kernel<false><<<grid, kDecodeThreads, 0, st>>>(p);
+  launch_decode(p, batch, false, static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return GDN_B200_OK;
@@ -186,23 +187,21 @@ extern "C" int gdn_b200_decode_pool(const void* q, const void* k, const void* v,
   if (batch < 0) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch must be >= 0");
   if (seq_len < 1 || seq_len > 0x7fffffffLL)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "seq_len must be in [1, 2^31)");
-  if (batch * num_v_heads * (kHeadDim / 16) > 0x7fffffffLL)
+  if (batch * num_v_heads * decode_ctas_per_head<float>() > 0x7fffffffLL)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "batch * num_v_heads exceeds the grid limit");
   if (batch == 0) return GDN_B200_OK;
   if (pool_size < 1) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "pool_size must be >= 1");
+  if (!aligned(v, 2) || !aligned(a, 2) || !aligned(b, 2))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "v/a/b need 2-byte alignment");
   if (!q || !k || !v || !state_pool || !new_state_pool || !read_indices || !A_log || !a ||
       !dt_bias || !b || !output)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null pointer argument");
-  const int state_align = state_is_bf16 ? 8 : 16;
-  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(state_pool, state_align) ||
-      !aligned(new_state_pool, state_align) ||
-      (intermediate_states && !aligned(intermediate_states, state_align)))
-    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
-                "q/k need 8-byte alignment and the state buffers 16-byte (fp32) or "
-                "8-byte (bf16) alignment");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(state_pool, 16) ||
+      !aligned(new_state_pool, 16) || (intermediate_states && !aligned(intermediate_states, 16)))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "q/k and the state buffers need 16-byte alignment");
   unsigned int* status = nullptr;
   if (int rc = device_setup(&status)) return rc;
-  PoolDecodeParams p;
+  DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k);
   p.v = static_cast<const __nv_bfloat16*>(v);
@@ -223,12 +222,7 @@ extern "C" int gdn_b200_decode_pool(const void* q, const void* k, const void* v,
   p.T = static_cast<int>(seq_len);
   p.h_qk = num_qk_heads;
   p.h_v = num_v_heads;
-  const dim3 grid(static_cast<unsigned>(batch * num_v_heads * (kHeadDim / 16)));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (state_is_bf16)
-    gdn_decode_pool_kernel<__nv_bfloat16><<<grid, kDecodeThreads, 0, st>>>(p);
-  else
-    gdn_decode_pool_kernel<float><<<grid, kDecodeThreads, 0, st>>>(p);
+  launch_decode(p, batch, state_is_bf16 != 0, static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "pooled decode launch");
   return GDN_B200_OK;
