@@ -49,6 +49,7 @@ _SIGNATURES = {
                                                ctypes.c_int32, ctypes.c_double, _P, _P,
                                                ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_int32, _P]),
+    "gdn_b200_state_affine": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64, _P]),
     "gdn_b200_device_status": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32),
                                               ctypes.c_int32]),
     "gdn_b200_last_error": (ctypes.c_char_p, []),

@@ -60,7 +60,7 @@ def _sources(*names):
 def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> list:
     """Compile every shared library of the package; returns their paths."""
     core_deps = _sources("gdn_b200.cu", "gdn_ptx.cuh", "decode_kernel.cuh", "prefill_kernel.cuh",
-                         "prefill_split.cuh")
+                         "prefill_split.cuh", "state_affine_kernel.cuh")
     core_deps.append(os.path.join(INCLUDE, "gdn_b200.h"))
     if force or _stale(LIB, core_deps):
         cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, f"-I{INCLUDE}", "-o", LIB,

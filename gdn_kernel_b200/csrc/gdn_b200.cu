@@ -13,6 +13,7 @@
 #include "gdn_b200.h"
 #include "decode_kernel.cuh"
 #include "prefill_split.cuh"
+#include "state_affine_kernel.cuh"
 
 namespace gdn {
 
@@ -225,6 +226,26 @@ extern "C" int gdn_b200_decode_pool(const void* q, const void* k, const void* v,
   launch_decode(p, batch, state_is_bf16 != 0, static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "pooled decode launch");
+  return GDN_B200_OK;
+}
+
+extern "C" int gdn_b200_state_affine(const float* state, const float* transfer,
+                                     const float* offset, float* out, int64_t num_heads,
+                                     void* stream) {
+  t_last_error.clear();
+  if (num_heads < 0 || num_heads > 65535)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_heads must be in [0, 65535]");
+  if (num_heads == 0) return GDN_B200_OK;
+  if (!offset || !out || (state && !transfer))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (out == state || out == transfer)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "out must not alias state or transfer");
+  const dim3 grid((kHeadDim / kAffineTile) * (kHeadDim / kAffineTile),
+                  static_cast<unsigned>(num_heads));
+  gdn_state_affine_kernel<<<grid, kAffineThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      state, transfer, offset, out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "state affine launch");
   return GDN_B200_OK;
 }
 

@@ -181,6 +181,24 @@ def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, sca
     return output, final_state
 
 
+def state_affine(state, transfer, offset, out=None):
+    """``out[h] = state[h] @ transfer[h] + offset[h]`` for [H, 128, 128] fp32 CUDA
+    tensors (``state`` None means zero): the affine combine of context-parallel
+    prefill.  Returns ``out`` (allocated when omitted)."""
+    dev = _cuda_device(offset)
+    H = offset.shape[0]
+    _check(offset, "offset", torch.float32, (H, HEAD_DIM, HEAD_DIM), dev)
+    if state is not None:
+        _check(state, "state", torch.float32, (H, HEAD_DIM, HEAD_DIM), dev)
+        _check(transfer, "transfer", torch.float32, (H, HEAD_DIM, HEAD_DIM), dev)
+    if out is None:
+        out = torch.empty_like(offset)
+    _check(out, "out", torch.float32, (H, HEAD_DIM, HEAD_DIM), dev)
+    _lib.check(_lib.load().gdn_b200_state_affine(_ptr(state), _ptr(transfer), _ptr(offset),
+                                                 _ptr(out), H, _stream(dev)))
+    return out
+
+
 PREFILL_PATHS = ("split", "fused")
 
 

@@ -129,6 +129,20 @@ int gdn_b200_prefill_ws(const void* q, const void* k, const void* v, const float
                         int32_t num_v_heads, int32_t head_dim,
                         void* workspace, uint64_t workspace_bytes, void* stream);
 
+/*
+ * Affine state combine of the context-parallel prefill, per head:
+ *   out[h] = state[h] * transfer[h] + offset[h]     (128 x 128 fp32, row = v)
+ * Over a segment of a sequence the chunked recurrence maps every state row the
+ * same affine way, S_end = S_0 * M + N (M: the segment's transfer, the final state
+ * of a V = 0 run from the identity; N: its offset, the final state of a run from
+ * the zero state), so a rank learns its segment's initial state by folding the
+ * (M, N) of the segments before it.  state == NULL means a zero state (out =
+ * offset).  out may alias offset but not state or transfer.  All [num_heads, 128,
+ * 128] fp32.  No counterpart in the reference, which is single-GPU.
+ */
+int gdn_b200_state_affine(const float* state, const float* transfer, const float* offset,
+                          float* out, int64_t num_heads, void* stream);
+
 /* Capacity (bytes) of the scratch array that gdn_b200_prefill_static uses. */
 #define GDN_B200_PREFILL_STATIC_SCRATCH_BYTES (64ull << 20)
 

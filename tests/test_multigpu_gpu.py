@@ -39,3 +39,18 @@ def test_two_gpu_decode_equals_one_gpu():
                         first.dt_bias.cuda(), b.cuda(), first.scale, in_place=True)
         ref.append(o.cpu())
     assert torch.equal(outs, torch.stack(ref)) and torch.equal(state, st.cpu())
+
+
+def test_two_gpu_context_parallel_prefill():
+    """One 333-token sequence split over 2 GPUs (NCCL all-gather of the segment
+    maps) against the fp32 oracle of the whole sequence."""
+    _need_two()
+    from helpers import assert_prefill_close
+    from oracle import gdn_oracle as O
+    res = S.launch_workers(DW.gpu_cp_worker, 2, backend="nccl", timeout_s=300)
+    assert all(r.ok for r in res), [r.error for r in res]
+    out, end = res[0].value
+    x = DW._cp_inputs()
+    ro, rs = O.prefill_chunked(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b,
+                               x.cu_seqlens, x.scale)
+    assert_prefill_close(out, end[None], ro, rs)
