@@ -10,6 +10,8 @@ Also reported on the same line:
 * ``prefill``: configs[2] (one 8192-token sequence, chunked C=64) tokens/s and
   its tensor/HBM roofline, plus configs[3] (16 packed sequences) tokens/s;
 * ``decode_sweep``: configs[1] B in {1, 8, 32, 64, 128, 256};
+* ``sharded``: BASELINE configs[4] over the ranks (decode B=1024, 64-sequence
+  prefill) and one 65,536-token sequence by context-parallel prefill;
 * ``decode_pool``: the pooled / multi-token decode at B=64 (fp32 and bf16 state
   pools, T=1 and T=4, with and without per-token intermediate states);
 * ``roofline``: the decode kernel against the measured HBM copy bandwidth;
@@ -309,7 +311,58 @@ def run_sharded(K, rank, world, flush, hbm_peak):
                             "hbm_GBps": round(hb / (pms * 1e-3) / 1e9, 1),
                             "box_frac_hbm": round(hb / (pms * 1e-3) / 1e9 / (world * hbm_peak), 4),
                             "tokens_this_rank": sum(mine)}
+    # (c) one long sequence split over the ranks (context-parallel prefill; one
+    # all-gather of the per-segment affine state maps per call)
+    res["prefill_context_parallel"] = time_context_parallel(K, rank, world, flush, 65536)
     return res
+
+
+def time_context_parallel(K, rank, world, flush, total_tokens, iters=3, warmup=1):
+    """One sequence of ``total_tokens`` tokens: the single-call prefill at one
+    GPU, the context-parallel prefill over ``world`` ranks otherwise (device
+    time per call, max over ranks)."""
+    from gdn_kernel_b200 import context_parallel as CP, workloads as W
+    import torch.distributed as dist
+
+    x = W.make_prefill_inputs([total_tokens], seed=6100, device="cuda")
+    lo, hi = CP.cp_segments(total_tokens, world)[rank]
+    if world == 1:
+        out = torch.empty(total_tokens, H_V, D, dtype=torch.bfloat16, device="cuda")
+        ns = torch.empty(1, H_V, D, D, dtype=torch.float32, device="cuda")
+        ws = torch.empty(K.prefill_workspace_bytes(1, total_tokens, H_V), dtype=torch.uint8,
+                         device="cuda")
+
+        def run():
+            K.gdn_prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
+                          x.scale, out, ns, workspace=ws)
+    else:
+        seg = lambda t: t[lo:hi].contiguous()
+        q, k, v, a, b = (seg(t) for t in (x.q, x.k, x.v, x.a, x.b))
+
+        def run():
+            CP.cp_prefill(rank, world, q, k, v, x.state[0], x.A_log, a, x.dt_bias, b, x.scale)
+    for _ in range(warmup):
+        flush.zero_()
+        run()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        flush.zero_()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = _events()
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ms = _max_over_ranks(statistics.median(ts), world)
+    del x
+    return {"tokens": total_tokens, "us": round(ms * 1e3, 1),
+            "tokens_per_s": round(total_tokens / (ms * 1e-3), 1),
+            "segment_tokens_this_rank": hi - lo,
+            "method": "single call" if world == 1 else
+                      f"context-parallel over {world} ranks (pass A, all-gather, pass B)"}
 
 
 def prefill_hbm_bytes(lengths, with_state):

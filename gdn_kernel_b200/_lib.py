@@ -49,6 +49,14 @@ _SIGNATURES = {
                                                ctypes.c_int32, ctypes.c_double, _P, _P,
                                                ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_int32, _P]),
+    "gdn_b200_prefill_prepare": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, ctypes.c_int32,
+                                                ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                                ctypes.c_int32, ctypes.c_int32, _P,
+                                                ctypes.c_uint64, _P]),
+    "gdn_b200_prefill_recur": (ctypes.c_int, [_P, _P, _P, ctypes.c_double, _P, _P,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_uint64,
+                                              _P]),
     "gdn_b200_state_affine": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64, _P]),
     "gdn_b200_device_status": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32),
                                               ctypes.c_int32]),

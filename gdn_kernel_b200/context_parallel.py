@@ -8,25 +8,29 @@ state row evolves by the same affine map, ``S_end = S_0 @ M + N`` (row = v,
 k-last layout; the per-chunk map is ``e^{gamma_last} I - W^T K_decay``, ref
 solution/cuda/kernel_prefill.cu:286-293), so each rank
 
-1. runs pass A, one packed prefill of two copies of its segment: the real V
-   from a zero state (final state = the offset N) and V = 0 from the identity
-   (final state = the transfer M);
+1. prepares its segment once (chunk table and per-chunk records, which do not
+   depend on V or on the state) and runs pass A, two recurrences over the
+   prepared segment on two streams: the real V from a zero state (final state
+   = the offset N) and V = 0 from the identity (final state = the transfer M);
 2. all-gathers (M, N) across the ranks: 2 x H_v x 64 KiB per rank, the only
    exchange, issued once per call;
 3. folds the maps of the segments before it into its true initial state,
    ``S_g = S_{g-1} @ M_{g-1} + N_{g-1}`` (``gdn_b200_state_affine``), starting
    from the sequence's initial state;
-4. runs pass B, the prefill of its segment from ``S_g``, giving its outputs and
-   the state at its segment's end (on the last rank: the sequence's final state).
+4. runs pass B, the recurrence of its segment from ``S_g`` over the same
+   prepared records, giving its outputs and the state at its segment's end (on
+   the last rank: the sequence's final state).
 
-Each rank therefore does about three segment-prefills of work (pass A is one
-call over twice the tokens) instead of the whole chain, and the per-head
+Each rank therefore prepares T/G tokens once and runs three recurrences over
+them (two of them concurrently) instead of the whole chain, and the per-head
 sequential depth drops from T/64 chunks to about 2T/(64 G).  The reference is
 single-GPU (its harness requests one B200, ref scripts/run_modal.py:36); this
 is the split its recurrence admits.
 
-The compute functions are parameters so that the host logic runs in CPU tests
-with the fp32 oracle standing in for the CUDA kernels.
+The compute is a parameter: ``prefill_fn`` (a full prefill with the reference
+``kernel`` signature) switches to the generic form of passes A and B through
+that function, which is how the host logic runs in CPU tests with the fp32
+oracle standing in for the CUDA kernels.
 """
 
 from __future__ import annotations
@@ -94,6 +98,64 @@ def fold_states(state0: Optional[torch.Tensor], maps, affine_fn: Optional[Callab
     return s
 
 
+class _KernelSegment:
+    """Passes A and B with the CUDA kernels: one prepare, three recurrences."""
+
+    def __init__(self, q, k, v, A_log, a, dt_bias, b, scale):
+        from . import kernel as K
+        self.K, self.k, self.v, self.scale = K, k, v, scale
+        T, _, D = q.shape
+        self.h_v, self.D = v.shape[1], D
+        cu = torch.tensor([0, T], dtype=torch.int32, device=q.device)
+        self.ws = torch.empty(K.prefill_workspace_bytes(1, T, self.h_v), dtype=torch.uint8,
+                              device=q.device)
+        K.gdn_prefill_prepare(q, k, A_log, a, dt_bias, b, cu, self.ws)
+
+    def maps(self):
+        K, dev, h_v, D = self.K, self.k.device, self.h_v, self.D
+        n = torch.empty(1, h_v, D, D, dtype=torch.float32, device=dev)
+        m = torch.empty(1, h_v, D, D, dtype=torch.float32, device=dev)
+        eye = torch.eye(D, dtype=torch.float32, device=dev).expand(1, h_v, D, D).contiguous()
+        main = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(main)
+        K.gdn_prefill_recur(self.k, self.v, None, self.scale, None, n, 1, h_v, self.ws)
+        with torch.cuda.stream(side):
+            K.gdn_prefill_recur(self.k, None, eye, self.scale, None, m, 1, h_v, self.ws)
+        main.wait_stream(side)
+        return m[0], n[0]
+
+    def run(self, state):
+        K, dev = self.K, self.k.device
+        out = torch.empty(self.k.shape[0], self.h_v, self.D, dtype=torch.bfloat16, device=dev)
+        ns = torch.empty(1, self.h_v, self.D, self.D, dtype=torch.float32, device=dev)
+        K.gdn_prefill_recur(self.k, self.v, state.unsqueeze(0).contiguous(), self.scale, out, ns,
+                            1, self.h_v, self.ws)
+        return out, ns[0]
+
+
+class _FunctionSegment:
+    """Passes A and B through a full prefill function (reference signature)."""
+
+    def __init__(self, prefill_fn, q, k, v, A_log, a, dt_bias, b, scale):
+        self.fn = prefill_fn
+        self.args = (q, k, v, A_log, a, dt_bias, b, scale)
+
+    def maps(self):
+        return segment_affine(*self.args, prefill_fn=self.fn)
+
+    def run(self, state):
+        q, k, v, A_log, a, dt_bias, b, scale = self.args
+        T, _, D = q.shape
+        h_v = v.shape[1]
+        out = torch.empty(T, h_v, D, dtype=torch.bfloat16, device=q.device)
+        ns = torch.empty(1, h_v, D, D, dtype=torch.float32, device=q.device)
+        cu = torch.tensor([0, T], dtype=torch.int32, device=q.device)
+        self.fn(q, k, v, state.unsqueeze(0).contiguous(), A_log, a, dt_bias, b, cu, scale, out,
+                ns)
+        return out, ns[0]
+
+
 def cp_prefill(rank: int, world: int, q, k, v, state, A_log, a, dt_bias, b, scale, *,
                prefill_fn: Optional[Callable] = None, affine_fn: Optional[Callable] = None,
                group=None):
@@ -108,26 +170,24 @@ def cp_prefill(rank: int, world: int, q, k, v, state, A_log, a, dt_bias, b, scal
     """
     import torch.distributed as dist
 
-    prefill_fn = prefill_fn or _default_prefill()
     T, _, D = q.shape
     h_v = v.shape[1]
     dev = q.device
+    seg = None
     if T > 0:
-        m, n = segment_affine(q, k, v, A_log, a, dt_bias, b, scale, prefill_fn)
+        seg = (_FunctionSegment(prefill_fn, q, k, v, A_log, a, dt_bias, b, scale)
+               if prefill_fn is not None
+               else _KernelSegment(q, k, v, A_log, a, dt_bias, b, scale))
+        m, n = seg.maps()
     else:   # an empty segment maps every state to itself
         m = torch.eye(D, dtype=torch.float32, device=dev).expand(h_v, D, D).contiguous()
         n = torch.zeros(h_v, D, D, dtype=torch.float32, device=dev)
     mine = torch.stack([m, n])
     parts = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(parts, mine, group=group)
-    s0 = state if state is not None else None
-    s_in = fold_states(s0, [(p[0], p[1]) for p in parts[:rank]], affine_fn)
+    s_in = fold_states(state, [(p[0], p[1]) for p in parts[:rank]], affine_fn)
     if s_in is None:
         s_in = torch.zeros(h_v, D, D, dtype=torch.float32, device=dev)
-    out = torch.empty(T, h_v, D, dtype=torch.bfloat16, device=dev)
-    if T == 0:
-        return out, s_in.clone()
-    ns = torch.empty(1, h_v, D, D, dtype=torch.float32, device=dev)
-    cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
-    prefill_fn(q, k, v, s_in.unsqueeze(0).contiguous(), A_log, a, dt_bias, b, cu, scale, out, ns)
-    return out, ns[0]
+    if seg is None:
+        return torch.empty(0, h_v, D, dtype=torch.bfloat16, device=dev), s_in.clone()
+    return seg.run(s_in)

@@ -309,6 +309,58 @@ int prefill_setup(const void* q, const void* k, const void* v, const float* stat
   return GDN_B200_OK;
 }
 
+// Checks shared by the two-stage entry points that take a caller workspace.
+int check_two_stage(int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                    int32_t num_v_heads, int32_t head_dim, const void* workspace,
+                    uint64_t workspace_bytes) {
+  if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
+  if (num_seqs < 0 || total_tokens < 0)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0");
+  if (num_seqs > 65535) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs exceeds 65535");
+  if (total_tokens > 0x7fffffffLL - kChunk)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "total_tokens exceeds the int32 TMA coordinate range");
+  if (num_seqs == 0) return GDN_B200_OK;
+  const SplitLayout L = split_layout(num_seqs, total_tokens, num_v_heads);
+  if (!workspace || workspace_bytes < L.total || !aligned(workspace, 256))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "workspace is null, not 256-byte aligned or smaller than "
+                "gdn_b200_prefill_workspace_size()");
+  if (L.max_chunks > 0x7fffffffLL) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "too many chunks");
+  return GDN_B200_OK;
+}
+
+SplitParams split_params(const PrefillParams& p, void* workspace, const SplitLayout& L,
+                         int64_t num_seqs, int zero_v) {
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  SplitParams sp;
+  sp.base = p;
+  sp.zero_v = zero_v;
+  sp.header = reinterpret_cast<int*>(ws + L.off_header);
+  sp.seq_off = reinterpret_cast<int*>(ws + L.off_seq);
+  sp.table = reinterpret_cast<ChunkInfo*>(ws + L.off_table);
+  sp.records = ws + L.off_rec;
+  sp.num_seqs = static_cast<int>(num_seqs);
+  sp.max_chunks = static_cast<int>(L.max_chunks);
+  return sp;
+}
+
+// Chunk table and per-(chunk, v-head) records into the workspace.
+void launch_prepare(const SplitParams& sp, const CUtensorMap& tq, const CUtensorMap& tk,
+                    const SplitLayout& L, int32_t num_v_heads, cudaStream_t st) {
+  gdn_chunk_table_kernel<<<1, kTableThreads, 0, st>>>(sp);
+  if (L.max_chunks > 0) {
+    const dim3 g1(static_cast<unsigned>(L.max_chunks), static_cast<unsigned>(num_v_heads));
+    gdn_prefill_prep_kernel<<<g1, kPrefillThreads, kP1Smem, st>>>(tq, tk, sp);
+  }
+}
+
+// The state recurrence over a prepared workspace (reads it only).
+void launch_recur(const SplitParams& sp, const CUtensorMap& tk, const CUtensorMap& tv,
+                  int64_t num_seqs, int32_t num_v_heads, cudaStream_t st) {
+  const dim3 g2(static_cast<unsigned>(2 * num_v_heads), static_cast<unsigned>(num_seqs));
+  gdn_prefill_chain_kernel<<<g2, kC2Threads, kC2Smem, st>>>(tk, tv, sp);
+}
+
 }  // namespace
 }  // namespace gdn
 
@@ -363,25 +415,109 @@ extern "C" int gdn_b200_prefill_ws(const void* q, const void* k, const void* v,
                 "gdn_b200_prefill_workspace_size()");
   if (L.max_chunks > 0x7fffffffLL)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "too many chunks");
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  SplitParams sp;
-  sp.base = p;
-  sp.header = reinterpret_cast<int*>(ws + L.off_header);
-  sp.seq_off = reinterpret_cast<int*>(ws + L.off_seq);
-  sp.table = reinterpret_cast<ChunkInfo*>(ws + L.off_table);
-  sp.records = ws + L.off_rec;
-  sp.num_seqs = static_cast<int>(num_seqs);
-  sp.max_chunks = static_cast<int>(L.max_chunks);
+  const SplitParams sp = split_params(p, workspace, L, num_seqs, 0);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  gdn_chunk_table_kernel<<<1, kTableThreads, 0, st>>>(sp);
-  if (L.max_chunks > 0) {
-    const dim3 g1(static_cast<unsigned>(L.max_chunks), static_cast<unsigned>(num_v_heads));
-    gdn_prefill_prep_kernel<<<g1, kPrefillThreads, kP1Smem, st>>>(tq, tk, sp);
-  }
-  const dim3 g2(static_cast<unsigned>(2 * num_v_heads), static_cast<unsigned>(num_seqs));
-  gdn_prefill_chain_kernel<<<g2, kC2Threads, kC2Smem, st>>>(tk, tv, sp);
+  launch_prepare(sp, tq, tk, L, num_v_heads, st);
+  launch_recur(sp, tk, tv, num_seqs, num_v_heads, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill (two-stage) launch");
+  return GDN_B200_OK;
+}
+
+extern "C" int gdn_b200_prefill_prepare(const void* q, const void* k, const float* A_log,
+                                        const void* a, const float* dt_bias, const void* b,
+                                        const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                                        int64_t num_seqs, int64_t total_tokens,
+                                        int32_t num_qk_heads, int32_t num_v_heads,
+                                        int32_t head_dim, void* workspace,
+                                        uint64_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  if (int rc = check_two_stage(num_seqs, total_tokens, num_qk_heads, num_v_heads, head_dim,
+                               workspace, workspace_bytes))
+    return rc;
+  if (num_seqs == 0) return GDN_B200_OK;
+  if (!cu_seqlens || !A_log || !dt_bias)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (total_tokens > 0 && (!q || !k || !a || !b))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null token tensor with total_tokens > 0");
+  if (total_tokens > 0 && (!aligned(q, 16) || !aligned(k, 16)))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "q/k need 16-byte alignment");
+  if (!aligned(cu_seqlens, cu_seqlens_is_int64 ? 8 : 4))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "cu_seqlens is misaligned");
+  unsigned int* status = nullptr;
+  if (int rc = device_setup(&status)) return rc;
+  CUtensorMap tq, tk;
+  const long long map_tokens = total_tokens > 0 ? total_tokens : 1;
+  const void* qb = total_tokens > 0 ? q : workspace;
+  const void* kb = total_tokens > 0 ? k : workspace;
+  const int hm = total_tokens > 0 ? num_qk_heads : 1;
+  if (int rc = make_token_map(&tq, qb, hm, map_tokens)) return rc;
+  if (int rc = make_token_map(&tk, kb, hm, map_tokens)) return rc;
+  PrefillParams p{};
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.cu_seqlens = cu_seqlens;
+  p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
+  p.total_tokens = total_tokens;
+  p.h_qk = num_qk_heads;
+  p.h_v = num_v_heads;
+  p.status = status;
+  const SplitLayout L = split_layout(num_seqs, total_tokens, num_v_heads);
+  const SplitParams sp = split_params(p, workspace, L, num_seqs, 0);
+  launch_prepare(sp, tq, tk, L, num_v_heads, static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill prepare launch");
+  return GDN_B200_OK;
+}
+
+extern "C" int gdn_b200_prefill_recur(const void* k, const void* v, const float* state,
+                                      double scale, void* output, float* new_state,
+                                      int64_t num_seqs, int64_t total_tokens,
+                                      int32_t num_qk_heads, int32_t num_v_heads,
+                                      int32_t head_dim, const void* workspace,
+                                      uint64_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  if (int rc = check_two_stage(num_seqs, total_tokens, num_qk_heads, num_v_heads, head_dim,
+                               workspace, workspace_bytes))
+    return rc;
+  if (num_seqs == 0) return GDN_B200_OK;
+  if (!new_state) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (total_tokens > 0 && !k)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "null k with total_tokens > 0");
+  if ((total_tokens > 0 && (!aligned(k, 16) || (v && !aligned(v, 16)) ||
+                            (output && !aligned(output, 16)))) ||
+      !aligned(new_state, 16) || (state && !aligned(state, 16)))
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "k/v/output/state/new_state need 16-byte alignment");
+  unsigned int* status = nullptr;
+  if (int rc = device_setup(&status)) return rc;
+  CUtensorMap tk, tv;
+  const long long map_tokens = total_tokens > 0 ? total_tokens : 1;
+  const void* kb = total_tokens > 0 ? k : workspace;
+  if (int rc = make_token_map(&tk, kb, total_tokens > 0 ? num_qk_heads : 1, map_tokens)) return rc;
+  // With zero V the V map is never read; it describes k's memory to stay valid.
+  if (total_tokens > 0 && v) {
+    if (int rc = make_token_map(&tv, v, num_v_heads, map_tokens)) return rc;
+  } else {
+    tv = tk;
+  }
+  PrefillParams p{};
+  p.state = state;
+  p.total_tokens = total_tokens;
+  p.scale = resolve_scale(scale);
+  p.out = static_cast<__nv_bfloat16*>(output);
+  p.new_state = new_state;
+  p.h_qk = num_qk_heads;
+  p.h_v = num_v_heads;
+  p.status = status;
+  const SplitLayout L = split_layout(num_seqs, total_tokens, num_v_heads);
+  const SplitParams sp =
+      split_params(p, const_cast<void*>(workspace), L, num_seqs, v == nullptr ? 1 : 0);
+  launch_recur(sp, tk, tv, num_seqs, num_v_heads, static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill recurrence launch");
   return GDN_B200_OK;
 }
 

@@ -68,6 +68,7 @@ __host__ __device__ inline SplitLayout split_layout(long long num_seqs, long lon
 
 struct SplitParams {
   PrefillParams base;
+  int zero_v;             // chain kernel: V is all zero (no V tiles, no M1); out may be null
   int* header;            // [0] = total chunks
   int* seq_off;           // [N + 1] first chunk of each sequence
   ChunkInfo* table;       // [max_chunks]
@@ -453,11 +454,12 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     uint64_t* bar = bars + kC2BarLdA + st;
     const uint8_t* rec =
         sp.records + (static_cast<size_t>(gc0 + c) * p.h_v + head) * kRecBytes;
-    mbar_arrive_expect_tx(bar, kC2LoadA);
+    mbar_arrive_expect_tx(bar, sp.zero_v ? kC2LoadA - 8192 : kC2LoadA);
     bulk_load(stage + kC2StQW, rec + kRecOffQW, 32768, bar);
     bulk_load(stage + kC2StPT, rec + kRecOffP, 16384, bar);
     bulk_load(stage + kC2StGam, rec + kRecOffGam, 256, bar);
-    tma_load_3d(stage + kC2StV, &tm_v, bar, 64 * vs, head, static_cast<int>(cstart0 + 64 * c));
+    if (!sp.zero_v)
+      tma_load_3d(stage + kC2StV, &tm_v, bar, 64 * vs, head, static_cast<int>(cstart0 + 64 * c));
   };
   auto load_b = [&](int c) {   // K of chunk c -> stage c & 1
     const int st = c & 1;
@@ -569,18 +571,21 @@ __global__ void __launch_bounds__(kC2Threads, 1)
       uint8_t* stage = smem + st * kC2Stage;
       const int clen = chunk_len(c);
       if (!(ok = warp_wait(kC2BarLdA + st, (c >> 1) & 1, kStatusTmaTimeout))) break;
-      if (clen < kChunk) zero_rows(stage + kC2StV, 1, clen);
-      // M1 into D_UO[st] once the output warps have read its chunk c - 2
+      if (clen < kChunk && !sp.zero_v) zero_rows(stage + kC2StV, 1, clen);
+      // M1 into D_UO[st] once the output warps have read its chunk c - 2 (with
+      // zero V there is no M1; the commit then only orders the buffer's reuse)
       if (c >= 2 && !(ok = warp_wait(kC2BarOut + st, ((c - 2) >> 1) & 1, kStatusMmaTimeout)))
         break;
       tc_fence_after();
       if (elect_one()) {
         const uint32_t a_st = smem_u32(stage);
+        if (!sp.zero_v) {
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
-          umma_bf16(tmem + kC2TmUO + 64 * st, sdesc_sw128(a_st + kC2StPT + s * 32, 16, 1024),
-                    sdesc_sw128(a_st + kC2StV + s * 2048, 8192, 1024), idesc_uo,
-                    s > 0 ? 1u : 0u);
+          for (int s = 0; s < 4; ++s)
+            umma_bf16(tmem + kC2TmUO + 64 * st, sdesc_sw128(a_st + kC2StPT + s * 32, 16, 1024),
+                      sdesc_sw128(a_st + kC2StV + s * 2048, 8192, 1024), idesc_uo,
+                      s > 0 ? 1u : 0u);
+        }
         umma_commit(bars + kC2BarM1 + st);
       }
       __syncwarp();
@@ -625,7 +630,8 @@ __global__ void __launch_bounds__(kC2Threads, 1)
           for (int s = 0; s < 8; ++s)
             umma_bf16_elect(tmem + kC2TmUO + 64 * st,
                             sdesc_sw128(a_st + kC2StQW + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
-                            sdesc_sw128(a_sb + s * 2048, 16384, 1024), idesc_uo, 1u);
+                            sdesc_sw128(a_sb + s * 2048, 16384, 1024), idesc_uo,
+                            (s > 0 || !sp.zero_v) ? 1u : 0u);
           umma_commit_elect(bars + kC2BarUO + st);
         }
         ok = ok && warp_wait(kC2BarKReady + st, (c >> 1) & 1, kStatusTmaTimeout);
@@ -689,7 +695,7 @@ __global__ void __launch_bounds__(kC2Threads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + kC2BarOut + st);
-      if (orow < chunk_len(c)) {
+      if (p.out && orow < chunk_len(c)) {
         __nv_bfloat16* o = p.out + (static_cast<size_t>(cstart0 + 64 * c + orow) * p.h_v + head) *
                                        kHeadDim + 64 * vs;
 #pragma unroll

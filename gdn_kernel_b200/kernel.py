@@ -261,6 +261,50 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                                        _stream(dev)))
 
 
+def gdn_prefill_prepare(q, k, A_log, a, dt_bias, b, cu_seqlens, workspace) -> None:
+    """First stage of the two-stage prefill: the chunk table and the per-(chunk,
+    v-head) records into ``workspace`` (see ``prefill_workspace_bytes``); depends
+    on q, k, a, b and the head parameters only."""
+    dev = _cuda_device(q)
+    T, h_qk, D = q.shape
+    h_v = a.shape[1]
+    N = cu_seqlens.numel() - 1
+    _require(cu_seqlens.dtype in (torch.int32, torch.int64), "cu_seqlens must be int32 or int64")
+    _check(cu_seqlens, "cu_seqlens", cu_seqlens.dtype, (N + 1,), dev)
+    _check(q, "q", torch.bfloat16, (T, h_qk, D), dev)
+    _check(k, "k", torch.bfloat16, (T, h_qk, D), dev)
+    _check(A_log, "A_log", torch.float32, (h_v,), dev)
+    _check(a, "a", torch.bfloat16, (T, h_v), dev)
+    _check(dt_bias, "dt_bias", torch.float32, (h_v,), dev)
+    _check(b, "b", torch.bfloat16, (T, h_v), dev)
+    _lib.check(_lib.load().gdn_b200_prefill_prepare(
+        _ptr(q), _ptr(k), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b), _ptr(cu_seqlens),
+        1 if cu_seqlens.dtype == torch.int64 else 0, N, T, h_qk, h_v, D, _ptr(workspace),
+        workspace.numel() * workspace.element_size(), _stream(dev)))
+
+
+def gdn_prefill_recur(k, v, state, scale, output, new_state, num_seqs, num_v_heads,
+                      workspace) -> None:
+    """Second stage: the state recurrence over a workspace a preceding
+    ``gdn_prefill_prepare`` filled (read only, so several may run concurrently).
+    ``v`` None means zero values, ``output`` None skips the outputs, ``state``
+    None means zero initial states."""
+    dev = _cuda_device(k)
+    T, h_qk, D = k.shape
+    _check(k, "k", torch.bfloat16, (T, h_qk, D), dev)
+    if v is not None:
+        _check(v, "v", torch.bfloat16, (T, num_v_heads, D), dev)
+    if output is not None:
+        _check(output, "output", torch.bfloat16, (T, num_v_heads, D), dev)
+    _check(new_state, "new_state", torch.float32, (num_seqs, num_v_heads, D, D), dev)
+    if state is not None:
+        _check(state, "state", torch.float32, (num_seqs, num_v_heads, D, D), dev)
+    _lib.check(_lib.load().gdn_b200_prefill_recur(
+        _ptr(k), _ptr(v), _ptr(state), float(scale or 0.0), _ptr(output), _ptr(new_state),
+        num_seqs, T, h_qk, num_v_heads, D, _ptr(workspace),
+        workspace.numel() * workspace.element_size(), _stream(dev)))
+
+
 def decode(q, k, v, state, A_log, a, dt_bias, b, scale: float = 0.0, *, in_place: bool = False):
     """Allocating decode: returns ``(output, new_state)``; with ``in_place`` the
     new state is written into ``state``."""

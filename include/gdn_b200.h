@@ -143,6 +143,34 @@ int gdn_b200_prefill_ws(const void* q, const void* k, const void* v, const float
 int gdn_b200_state_affine(const float* state, const float* transfer, const float* offset,
                           float* out, int64_t num_heads, void* stream);
 
+/*
+ * The two stages of gdn_b200_prefill_ws as separate calls, so that one
+ * preparation serves several recurrences over the same tokens (the
+ * context-parallel prefill runs three: from the zero state, from the identity
+ * with zero values, and from the true initial state).  No counterpart in the
+ * reference, whose single kernel does both.
+ *
+ * gdn_b200_prefill_prepare writes the chunk table and the per-(chunk, v-head)
+ * records (everything that depends on q, k, a, b, A_log, dt_bias only) into
+ * `workspace` (same size and alignment rules as gdn_b200_prefill_ws).
+ *
+ * gdn_b200_prefill_recur runs the state recurrence over a workspace that a
+ * preceding gdn_b200_prefill_prepare with the same num_seqs / total_tokens /
+ * heads filled (earlier on the same stream, or ordered before it); it only
+ * reads the workspace, so recurrences may run concurrently on other streams.
+ * `k` must be the prepared k.  v == NULL means all-zero values; output == NULL
+ * skips the outputs; state == NULL means zero initial states.
+ */
+int gdn_b200_prefill_prepare(const void* q, const void* k, const float* A_log, const void* a,
+                             const float* dt_bias, const void* b, const void* cu_seqlens,
+                             int32_t cu_seqlens_is_int64, int64_t num_seqs, int64_t total_tokens,
+                             int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                             void* workspace, uint64_t workspace_bytes, void* stream);
+int gdn_b200_prefill_recur(const void* k, const void* v, const float* state, double scale,
+                           void* output, float* new_state, int64_t num_seqs, int64_t total_tokens,
+                           int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                           const void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* Capacity (bytes) of the scratch array that gdn_b200_prefill_static uses. */
 #define GDN_B200_PREFILL_STATIC_SCRATCH_BYTES (64ull << 20)
 

@@ -114,20 +114,21 @@ def _cp_inputs():
     return W.make_prefill_inputs([CP_TOKENS], seed=91, h_qk=1, h_v=2)
 
 
-def cp_worker(rank, world, device=None, prefill_fn=None, affine_fn=None):
-    """One context-parallel prefill of a single sequence split over the ranks;
-    rank 0 returns the reassembled outputs and the last rank's end state."""
+def cp_worker(rank, world, device=None, kernels=False):
+    """One context-parallel prefill of a single sequence split over the ranks
+    (the oracle as compute on CPU; the CUDA kernels with ``kernels``); rank 0
+    returns the reassembled outputs and the last rank's end state."""
     from gdn_kernel_b200 import context_parallel as CP
     x = _cp_inputs()
     lo, hi = CP.cp_segments(CP_TOKENS, world)[rank]
     dev = device or "cpu"
     seg = lambda t: t[lo:hi].contiguous().to(dev)
     state = x.state[0].to(dev)
+    extra = {} if kernels else dict(
+        prefill_fn=oracle_prefill_dps,
+        affine_fn=lambda s, m, n: n if s is None else s @ m + n)
     out, end = CP.cp_prefill(rank, world, seg(x.q), seg(x.k), seg(x.v), state, x.A_log.to(dev),
-                             seg(x.a), x.dt_bias.to(dev), seg(x.b), x.scale,
-                             prefill_fn=prefill_fn or oracle_prefill_dps,
-                             affine_fn=affine_fn or (lambda s, m, n: n if s is None
-                                                     else s @ m + n))
+                             seg(x.a), x.dt_bias.to(dev), seg(x.b), x.scale, **extra)
     parts = _gather((rank, out.cpu(), end.cpu()), world)
     if rank != 0:
         return None
@@ -136,7 +137,5 @@ def cp_worker(rank, world, device=None, prefill_fn=None, affine_fn=None):
 
 
 def gpu_cp_worker(rank, world):
-    from gdn_kernel_b200 import kernel as K
     torch.cuda.set_device(rank)
-    return cp_worker(rank, world, device=f"cuda:{rank}", prefill_fn=K.gdn_prefill,
-                     affine_fn=lambda s, m, n: K.state_affine(s, m, n))
+    return cp_worker(rank, world, device=f"cuda:{rank}", kernels=True)

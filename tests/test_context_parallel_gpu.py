@@ -26,6 +26,51 @@ def test_state_affine_kernel_matches_fp32_matmul():
     torch.testing.assert_close(n2.double(), ref, atol=1e-4, rtol=1e-5)
 
 
+def test_prepare_then_recur_equals_prefill():
+    """The two stages as separate calls give the single call's results bitwise;
+    a null V equals an all-zero V; a null output changes nothing else."""
+    lengths = [300, 0, 64, 1, 129]
+    x = W.make_prefill_inputs(lengths, seed=17, device="cuda")
+    T, N = sum(lengths), len(lengths)
+    ws = torch.empty(K.prefill_workspace_bytes(N, T, 32), dtype=torch.uint8, device="cuda")
+    K.gdn_prefill_prepare(x.q, x.k, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, ws)
+    out = torch.empty(T, 32, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty_like(x.state)
+    K.gdn_prefill_recur(x.k, x.v, x.state, x.scale, out, ns, N, 32, ws)
+    ro, rs = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
+                       x.scale)
+    assert torch.equal(out, ro) and torch.equal(ns, rs)
+    # the workspace is read only: a second recurrence from it gives the same again
+    ns2 = torch.empty_like(ns)
+    K.gdn_prefill_recur(x.k, x.v, x.state, x.scale, None, ns2, N, 32, ws)
+    assert torch.equal(ns2, rs)
+    zo, zs = (torch.empty_like(out), torch.empty_like(ns))
+    K.gdn_prefill_recur(x.k, torch.zeros_like(x.v), x.state, x.scale, zo, zs, N, 32, ws)
+    no = torch.full_like(out, 7.0)
+    nz = torch.empty_like(ns)
+    K.gdn_prefill_recur(x.k, None, x.state, x.scale, no, nz, N, 32, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(nz, zs) and torch.equal(no, zo)
+
+
+def test_kernel_segment_maps_match_function_maps():
+    """Pass A through prepare + two concurrent recurrences equals pass A
+    through one packed prefill call, and both are the segment's affine map."""
+    x = W.make_prefill_inputs([700], seed=23, device="cuda")
+    args = (x.q, x.k, x.v, x.A_log, x.a, x.dt_bias, x.b, x.scale)
+    m1, n1 = CP._KernelSegment(*args).maps()
+    m2, n2 = CP.segment_affine(*args)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(m1, m2, atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(n1, n2, atol=1e-6, rtol=1e-5)
+    s0 = x.state[0]
+    _, ref = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
+                       x.scale)
+    from helpers import rel_fro
+    err = rel_fro((s0 @ m1 + n1)[None].cpu(), ref.cpu())
+    assert err.max().item() < 1e-2
+
+
 def _emulate(x, world):
     T = x.q.shape[0]
     segs = CP.cp_segments(T, world)

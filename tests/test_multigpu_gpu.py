@@ -20,9 +20,11 @@ def test_two_gpu_prefill_equals_one_gpu():
     res = S.launch_workers(DW.gpu_prefill_worker, 2, timeout_s=300)
     assert all(r.ok for r in res), [r.error for r in res]
     out, ns = res[0].value
-    x = W.make_prefill_inputs(DW.PREFILL_LENGTHS, seed=77, h_qk=2, h_v=4, device="cuda")
-    ro, rs = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
-                       x.scale)
+    # the workers draw their inputs on the CPU (CPU and CUDA generators differ)
+    x = W.make_prefill_inputs(DW.PREFILL_LENGTHS, seed=77, h_qk=2, h_v=4)
+    c = lambda t: t.cuda()
+    ro, rs = K.prefill(c(x.q), c(x.k), c(x.v), c(x.state), c(x.A_log), c(x.a), c(x.dt_bias),
+                       c(x.b), c(x.cu_seqlens), x.scale)
     assert torch.equal(out, ro.cpu()) and torch.equal(ns, rs.cpu())
 
 
