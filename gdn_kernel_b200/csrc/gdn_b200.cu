@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -40,9 +41,17 @@ constexpr int kMaxDevices = 64;
 struct DeviceSetup {
   bool done = false;
   unsigned int* status = nullptr;
+  int sm_count = 0;
 };
 DeviceSetup g_setup[kMaxDevices];
 std::mutex g_setup_mu;
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  return g_setup[dev].sm_count > 0 ? g_setup[dev].sm_count : 148;
+}
 
 int device_setup(unsigned int** status_out) {
   int dev = 0;
@@ -64,6 +73,10 @@ int device_setup(unsigned int** status_out) {
     e = cudaFuncSetAttribute(gdn_prefill_chain_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kC2Smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem)");
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    s.sm_count = sms;
     s.status = static_cast<unsigned int*>(addr);
     s.done = true;
   }
@@ -349,8 +362,11 @@ void launch_prepare(const SplitParams& sp, const CUtensorMap& tq, const CUtensor
                     const SplitLayout& L, int32_t num_v_heads, cudaStream_t st) {
   gdn_chunk_table_kernel<<<1, kTableThreads, 0, st>>>(sp);
   if (L.max_chunks > 0) {
-    const dim3 g1(static_cast<unsigned>(L.max_chunks), static_cast<unsigned>(num_v_heads));
-    gdn_prefill_prep_kernel<<<g1, kPrefillThreads, kP1Smem, st>>>(tq, tk, sp);
+    // Persistent: two CTAs per SM (at most one per item) walk the items.
+    const long long items = L.max_chunks * static_cast<long long>(num_v_heads);
+    const long long ctas = std::min<long long>(items, 2LL * device_sm_count());
+    gdn_prefill_prep_kernel<<<static_cast<unsigned>(ctas), kPrefillThreads, kP1Smem, st>>>(
+        tq, tk, sp);
   }
 }
 

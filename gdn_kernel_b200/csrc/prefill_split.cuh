@@ -173,20 +173,30 @@ __device__ __forceinline__ void bulk_commit_and_wait_read() {
 }
 
 // ---------------------------------------------------------------- prep kernel
-constexpr uint32_t kP1OffQKW = 0;                      // 32 KiB [Q;K] then [e^g Q; -W]
-constexpr uint32_t kP1OffTPZT = 32768;                 // 32 KiB T' | P, then P T' | P' | T_b
-constexpr uint32_t kP1TbOff = 24576;                   // T_b within that region
-constexpr uint32_t kP1OffAF = 65536;
-constexpr uint32_t kP1OffTF = kP1OffAF + 64 * kLdA * 4;
-constexpr uint32_t kP1OffXS = kP1OffTF + 64 * kLdA * 4;
-constexpr uint32_t kP1OffGate = kP1OffXS + 32 * 40 * 4;   // gamma, beta, e^gamma [64]
-constexpr uint32_t kP1OffBar = kP1OffGate + 768;
-constexpr uint32_t kP1OffTmemPtr = kP1OffBar + 16;
+// Persistent: two CTAs per SM walk the (chunk, v-head) items in order (item =
+// chunk * H_v + head, so consecutive items share Q and K).  Two 35 KiB regions
+// take turns: the current item's [Q;K] tile lives in one while its fp32 A / T
+// scratch of the triangular solve lives in the other; once the solve is done
+// that scratch is dead, and the next item's Q/K copy lands there while this
+// item finishes its products and stores.  So the per-item path carries no copy
+// latency, no TMEM allocation and no store drain.
+constexpr uint32_t kP1Region = 35840;                   // 35 KiB: [Q;K] tile or A + T scratch
+constexpr uint32_t kP1OffR0 = 0;
+constexpr uint32_t kP1OffTPZT = kP1Region;             // 32 KiB T' | P, then P T' | P' | T_b
+constexpr uint32_t kP1OffR1 = kP1OffTPZT + 32768;
+constexpr uint32_t kP1TbOff = 24576;                   // T_b within TPZT
+constexpr uint32_t kP1OffTFinR = 64 * kLdA * 4;        // T after A within a scratch region
+constexpr uint32_t kP1OffXS = kP1OffR1 + kP1Region;
+constexpr uint32_t kP1OffGate = kP1OffXS + 32 * 40 * 4;   // 2 x (gamma, beta, e^gamma [64])
+constexpr uint32_t kP1OffBar = kP1OffGate + 2 * 768;      // TMA [2], MMA
+constexpr uint32_t kP1OffTmemPtr = kP1OffBar + 32;
 constexpr uint32_t kP1Smem = kP1OffTmemPtr + 16 + 1024;
 constexpr uint32_t kP1TmQK = 0;       // 64 columns
 constexpr uint32_t kP1TmX = 0;        // 128 columns (D_QK is consumed by then)
 constexpr uint32_t kP1TmW = 128;      // 128 columns
 constexpr uint32_t kP1TmCols = 256;
+static_assert(2 * kP1OffTFinR <= kP1Region, "A and T scratch must fit a region");
+static_assert(kP1Smem + 1024 <= 232448 / 2, "two prep CTAs must fit an SM");
 
 __global__ void __launch_bounds__(kPrefillThreads, 2)
     gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -195,25 +205,17 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const PrefillParams& p = sp.base;
-  const int gc = blockIdx.x, head = blockIdx.y;
-  const ChunkInfo info = sp.table[gc];
-  if (info.clen <= 0) return;   // slot past the last chunk
-  const int clen = info.clen;
-  const long long cstart = info.cstart;
-  const int hq = head / (p.h_v / p.h_qk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2, row = quad * 32 + lane;
+  const long long n_items = static_cast<long long>(sp.header[0]) * p.h_v;
 
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + kP1OffBar);
-  uint64_t* bar_mma = bar_tma + 1;
+  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + kP1OffBar);   // [2]
+  uint64_t* bar_mma = bar_tma + 2;
   uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + kP1OffTmemPtr);
-  float* AF = reinterpret_cast<float*>(smem + kP1OffAF);
-  float* TF = reinterpret_cast<float*>(smem + kP1OffTF);
   float* XS = reinterpret_cast<float*>(smem + kP1OffXS);
-  float* gam = reinterpret_cast<float*>(smem + kP1OffGate);
-  float* bet = gam + 64;
-  float* eg = gam + 128;
   uint8_t* tpzt = smem + kP1OffTPZT;
+  auto region = [&](int r) { return smem + (r ? kP1OffR1 : kP1OffR0); };
+  auto gates = [&](int r) { return reinterpret_cast<float*>(smem + kP1OffGate + 768 * r); };
 
   if (warp == 0) {
     tmem_alloc(tmem_ptr, kP1TmCols);
@@ -221,52 +223,98 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   }
   if (tid == 32) {
     mbar_init(bar_tma, 1);
+    mbar_init(bar_tma + 1, 1);
     mbar_init(bar_mma, 1);
     fence_mbarrier_init();
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
   }
   // The solve never writes the upper-right 32x32 blocks of the T' and T_b
-  // tiles (rows 0-31, 16-byte chunks 4-7): they hold zeros.
+  // tiles (rows 0-31, 16-byte chunks 4-7): they hold zeros for every item.
   {
     const int r = tid >> 3, c = 4 + ((tid >> 1) & 3), t = tid & 1;
     *reinterpret_cast<uint4*>(tpzt + 24576 * t + sw128_off(r, c)) = make_uint4(0, 0, 0, 0);
   }
-  __syncthreads();
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_tma, 4 * kTileBytes);
-    const int t0 = static_cast<int>(cstart);
-#pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
-      tma_load_3d(smem + kP1OffQKW + kb * 16384, &tm_q, bar_tma, kb * 64, hq, t0);
-      tma_load_3d(smem + kP1OffQKW + kb * 16384 + 8192, &tm_k, bar_tma, kb * 64, hq, t0);
-    }
-  }
-  if (warp == 1) {
-    const GateIn g = gate_inputs(p, cstart, clen, head, lane);
-    gate_finish(g, -expf(p.A_log[head]), p.dt_bias[head], lane, gam, bet, eg);
-  }
-  const bool ok = mbar_wait(bar_tma, 0);
-  unsigned int code = ok ? 0u : kStatusTmaTimeout;
-  if (clen < kChunk) {   // rows past the sequence end: zero Q and K rows
-    const int nrow = kChunk - clen;
-    for (int e = tid; e < 4 * nrow * 8; e += kPrefillThreads) {
-      const int reg = e / (nrow * 8);
-      const int r = clen + (e / 8) % nrow;
-      const uint32_t base = kP1OffQKW + (reg >> 1) * 16384 + (reg & 1) * 8192;
-      *reinterpret_cast<uint4*>(smem + base + sw128_off(r, e & 7)) = make_uint4(0, 0, 0, 0);
-    }
-  }
   fence_proxy_async_smem();
   tc_fence_before();
-  const bool fail0 = __syncthreads_or(!ok);
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_ptr;
   const uint32_t tm_lane = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t a_qkw = smem_u32(smem + kP1OffQKW);
   const uint32_t a_tpzt = smem_u32(tpzt);
 
-  if (!fail0) {
+  // Item `it`'s Q/K tiles into region r (thread 0); its gate inputs into warp
+  // 1's registers (finished into gate buffer r later, once they have landed).
+  auto issue_item = [&](long long it, const ChunkInfo& info, int r, GateIn& gi) {
+    const int head = static_cast<int>(it % p.h_v);
+    if (tid == 0) {
+      const int hq = head / (p.h_v / p.h_qk);
+      const int t0 = static_cast<int>(info.cstart);
+      mbar_arrive_expect_tx(bar_tma + r, 4 * kTileBytes);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb) {
+        tma_load_3d(region(r) + kb * 16384, &tm_q, bar_tma + r, kb * 64, hq, t0);
+        tma_load_3d(region(r) + kb * 16384 + 8192, &tm_k, bar_tma + r, kb * 64, hq, t0);
+      }
+    }
+    if (warp == 1) gi = gate_inputs(p, info.cstart, info.clen, head, lane);
+  };
+  auto finish_gates = [&](long long it, const GateIn& gi, int r) {
+    if (warp == 1) {
+      const int head = static_cast<int>(it % p.h_v);
+      float* g = gates(r);
+      gate_finish(gi, -expf(p.A_log[head]), p.dt_bias[head], lane, g, g + 64, g + 128);
+    }
+  };
+  auto table_at = [&](long long it) {
+    return it < n_items ? sp.table[static_cast<int>(it / p.h_v)] : ChunkInfo{-1, 0, 0};
+  };
+
+  unsigned int code = 0;
+  uint32_t mma_phase = 0;
+  bool failed = false;
+  int pend_r = -1;            // region whose copy is in flight and not yet waited for
+  uint32_t pend_parity = 0;
+  long long it = blockIdx.x;
+  ChunkInfo cur = table_at(it);
+  GateIn gi{};
+  if (it < n_items) {
+    issue_item(it, cur, 0, gi);
+    pend_r = 0;
+    pend_parity = 0;
+    finish_gates(it, gi, 0);
+  }
+  for (int j = 0; it < n_items; ++j, it += gridDim.x) {
+    const int r = j & 1;
+    const int gc = static_cast<int>(it / p.h_v), head = static_cast<int>(it % p.h_v);
+    const long long nxt = it + gridDim.x;
+    const ChunkInfo nxt_info = table_at(nxt);   // its latency hides behind this item
+    const int clen = cur.clen;
+    uint8_t* qkw = region(r);
+    float* AF = reinterpret_cast<float*>(region(r ^ 1));
+    float* TF = reinterpret_cast<float*>(region(r ^ 1) + kP1OffTFinR);
+    float* gam = gates(r);
+    float* bet = gam + 64;
+    float* eg = gam + 128;
+    const uint32_t a_qkw = smem_u32(qkw);
+
+    bool ok = mbar_wait(bar_tma + r, (j >> 1) & 1);
+    if (ok) pend_r = -1;
+    else code |= kStatusTmaTimeout;
+    if (clen < kChunk) {   // rows past the sequence end: zero Q and K rows
+      const int nrow = kChunk - clen;
+      for (int e = tid; e < 4 * nrow * 8; e += kPrefillThreads) {
+        const int reg = e / (nrow * 8);
+        const int rr = clen + (e / 8) % nrow;
+        *reinterpret_cast<uint4*>(qkw + (reg >> 1) * 16384 + (reg & 1) * 8192 +
+                                  sw128_off(rr, e & 7)) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) { failed = true; break; }   // also publishes the gates
+    tc_fence_after();
+
     // D_QK = [Q ; K] K^T, with K (rows 64-127 of the stacked tile) as the B operand.
     if (warp == 0) {
       if (elect_one()) {
@@ -281,7 +329,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
       }
       __syncwarp();
     }
-    if (!mbar_wait(bar_mma, 0)) code |= kStatusMmaTimeout;
+    // The previous item's records must have been read out of TPZT and the
+    // other region (its [Q;K] tile) before the P/A epilogue overwrites them.
+    if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    ok = mbar_wait(bar_mma, mma_phase & 1);
+    ++mma_phase;
+    if (!ok) code |= kStatusMmaTimeout;
+    if (__syncthreads_or(!ok)) { failed = true; break; }
     tc_fence_after();
     pa_epilogue(tmem + tm_lane + kP1TmQK, row, half, quad, clen, gam, bet, tpzt + 8192, AF);
     tc_fence_before();
@@ -290,6 +344,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
+    // The solve's scratch is dead: the next item's tiles go there now.
+    if (nxt < n_items) {
+      issue_item(nxt, nxt_info, r ^ 1, gi);
+      pend_r = r ^ 1;
+      pend_parity = ((j + 1) >> 1) & 1;
+    }
     // D_X = [P ; -] [T' | T_b]: P T' (columns 0-63) and P' = P T_b (64-127).
     // Rows 64-127 of the A operand are scratch; their products are not read.
     // The B operand's two 64-column blocks are the T' and T_b tiles.
@@ -306,15 +366,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
       __syncwarp();
     }
     if (quad < 2) {   // half 0: P T' over P (A rows 64-127 of D_W); half 1: P' to the scratch rows
-      if (!mbar_wait(bar_mma, 1)) code |= kStatusMmaTimeout;
+      if (!mbar_wait(bar_mma, mma_phase & 1)) code |= kStatusMmaTimeout;
       tc_fence_after();
-      float r[64];
-      tmem_ld64(tmem + tm_lane + kP1TmX + 64 * half, r);
-      st_row_bf16(tpzt + (half == 0 ? 8192 : 16384), row, r);
+      float rr[64];
+      tmem_ld64(tmem + tm_lane + kP1TmX + 64 * half, rr);
+      st_row_bf16(tpzt + (half == 0 ? 8192 : 16384), row, rr);
     }
+    ++mma_phase;
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    if (__syncthreads_or(code != 0)) { failed = true; break; }
     // D_W = [T' ; P T'] K, K the MN-major B operand (64-column blocks 16 KiB
     // apart): rows 0-63 W = T'K, rows 64-127 P W.
     if (warp == 0) {
@@ -329,30 +390,51 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
       }
       __syncwarp();
     }
-    if (!mbar_wait(bar_mma, 0)) code |= kStatusMmaTimeout;
+    ok = mbar_wait(bar_mma, mma_phase & 1);
+    ++mma_phase;
+    if (!ok) code |= kStatusMmaTimeout;
     tc_fence_after();
-    {
-      float r[64];
-      tmem_ld64(tmem + tm_lane + kP1TmW + 64 * half, r);
-      uint8_t* tile = smem + kP1OffQKW + half * 16384;
+    if (ok) {
+      float rr[64];
+      tmem_ld64(tmem + tm_lane + kP1TmW + 64 * half, rr);
+      uint8_t* tile = qkw + half * 16384;
       if (row < 64) {   // -W over the consumed K rows
-        st_half_row_bf16(tile, 64 + row, 0, r, -1.0f);
-        st_half_row_bf16(tile, 64 + row, 4, r + 32, -1.0f);
+        st_half_row_bf16(tile, 64 + row, 0, rr, -1.0f);
+        st_half_row_bf16(tile, 64 + row, 4, rr + 32, -1.0f);
       } else {          // Q' = e^gamma Q - P W over the Q rows
-        qprime_row(tile, row - 64, eg[row - 64], r);
+        qprime_row(tile, row - 64, eg[row - 64], rr);
       }
     }
+    // The next item's gates (its loads have landed by now) into the other buffer;
+    // that buffer's previous contents (item j - 1's gamma) were drained above.
+    if (nxt < n_items) finish_gates(nxt, gi, r ^ 1);
     fence_proxy_async_smem();
-    __syncthreads();
-    // Tile images out by bulk copies: [Q' ; -W], P', T_b, gamma.
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    tc_fence_after();
+    // Tile images out by bulk copies ([Q' ; -W], P', T_b, gamma); drained by
+    // the next item (or the end of the kernel) before their sources change.
     if (tid == 0) {
       uint8_t* rec = sp.records + (static_cast<size_t>(gc) * p.h_v + head) * kRecBytes;
-      bulk_store(rec + kRecOffQW, smem + kP1OffQKW, 32768);
+      bulk_store(rec + kRecOffQW, qkw, 32768);
       bulk_store(rec + kRecOffP, tpzt + 16384, 8192);
       bulk_store(rec + kRecOffTb, tpzt + kP1TbOff, 8192);
       bulk_store(rec + kRecOffGam, gam, 256);
-      bulk_commit_and_wait_read();
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
+    cur = nxt_info;
+  }
+  // Everything in flight lands before the CTA's shared memory and TMEM go
+  // away: bulk stores (thread 0's groups), and on a failed run the copy still
+  // pending and the tensor-core ops (one more bounded wait each).
+  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (failed) {
+    if (pend_r >= 0) mbar_wait(bar_tma + pend_r, pend_parity);
+    if (warp == 0) {
+      if (elect_one()) umma_commit(bar_mma);
+      __syncwarp();
+    }
+    mbar_wait(bar_mma, mma_phase & 1);
   }
   if (code) atomicOr(p.status, code);
   tc_fence_before();
