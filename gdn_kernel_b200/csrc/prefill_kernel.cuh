@@ -152,8 +152,35 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
 }
 
 // One 16x8 tile of D = L * R (L: 16 x 8*KSTEPS rows of pitch ldl; R: 8*KSTEPS x 8
-// of pitch ldr), one warp.  Lane (g = lane/4, t = lane%4) receives
+// of pitch ldr), one warp, in single TF32 (10-bit mantissa operands, fp32
+// accumulation).  Lane (g = lane/4, t = lane%4) receives
 // D[g][2t], D[g][2t+1], D[g+8][2t], D[g+8][2t+1].
+template <int KSTEPS>
+__device__ __forceinline__ void mma_tile_tf32(float (&d)[4], const float* L, int ldl,
+                                              const float* R, int ldr, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  float acc[KSTEPS][4];
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks) {
+    const uint32_t a[4] = {to_tf32(L[g * ldl + 8 * ks + t]), to_tf32(L[(g + 8) * ldl + 8 * ks + t]),
+                           to_tf32(L[g * ldl + 8 * ks + t + 4]),
+                           to_tf32(L[(g + 8) * ldl + 8 * ks + t + 4])};
+    const uint32_t b[2] = {to_tf32(R[(8 * ks + t) * ldr + g]), to_tf32(R[(8 * ks + t + 4) * ldr + g])};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[ks][e] = 0.f;
+    mma_tf32(acc[ks], a, b);
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float sum = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) sum += acc[ks][e];
+    d[e] = sum;
+  }
+}
+
+// The same tile in 3xTF32 (operands split into a TF32 head and tail; fp32-level
+// accuracy).
 template <int KSTEPS>
 __device__ __forceinline__ void mma_tile_3xtf32(float (&d)[4], const float* L, int ldl,
                                                 const float* R, int ldr, int lane) {
@@ -210,23 +237,30 @@ __device__ __forceinline__ void st_tp_pair(uint8_t* tpzt, int i, int j, float t0
   *reinterpret_cast<uint32_t*>(tpzt + off) = pack_bf16x2(b0 * eg[j], b1 * eg[j + 1]);
 }
 
-// T = (I - A)^{-1} for the strictly lower 64x64 fp32 A (row pitch kLdA):
-//   1. the two 32x32 diagonal blocks T_bb = (I - A_bb)^{-1}: warp b, lane j
-//      solves column j of block b by forward substitution with the column in
-//      registers (no barrier inside; the other warps wait at one barrier);
-//   2. T_10 = T_11 (A_10 T_00): two 32x32 products on the tensor cores in
-//      3xTF32 (fp32-level accuracy), one barrier apart.
-// Results go to T (fp32, read by step 2) and straight into the bf16 T' / T_b
-// operand tiles.  The upper-right 32x32 blocks of the T' / T_b tiles are never
-// written and must hold zeros; T's upper-right block is never read.
+// T = (I - A)^{-1} for the strictly lower 64x64 fp32 A (row pitch kLdA), by
+// block doubling from 16x16 diagonal blocks:
+//   1. the four 16x16 diagonal blocks T_bb = (I - A_bb)^{-1}: lanes 0-15 /
+//      16-31 of warps 0 and 1 each solve one column of one block by forward
+//      substitution with the column in registers;
+//   2. 16 -> 32: in each 32x32 diagonal block, T_10 = T_11 (A_10 T_00) as two
+//      16x16 products (warps 0-3, one 16x8 tile each);
+//   3. 32 -> 64: T_10 = T_11 (A_10 T_00) as two 32x32 products (all 8 warps).
+// The block products run on the tensor cores in single TF32: T is only used
+// through its bf16 copies (T', T_b), whose rounding (2^-9 relative) is coarser
+// than TF32's (2^-11), and the fp32 T only feeds these products.
+// Results go to T (fp32) and into the bf16 T' / T_b operand tiles.  The
+// upper-right 32x32 blocks of the T' / T_b tiles are never written and must
+// hold zeros; step 2 writes the zeros of the upper-right 16x16 blocks inside
+// the diagonal 32x32 blocks (T' / T_b and the fp32 T that step 3 reads).
 __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float* X, uint8_t* tpzt,
                                                  const float* bet, const float* eg, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
-  if (warp < 2) {   // step 1
-    const int o = 32 * warp, j = lane;
-    float x[32];
+  constexpr int kLdC = 40;    // pitch of the 32x32 scratch tile (conflict-free B fragments)
+  if (warp < 2) {   // step 1: block 2 warp + lane / 16, column lane % 16
+    const int o = 16 * (2 * warp + (lane >> 4)), j = lane & 15;
+    float x[16];
 #pragma unroll
-    for (int m = 0; m < 32; ++m) {
+    for (int m = 0; m < 16; ++m) {
       // four partial sums (one per float4 lane) keep the dependent FMA chain
       // of each row short; only the newest x enters through the last FMA
       float acc[4] = {(m == j) ? 1.0f : 0.0f, 0.f, 0.f, 0.f};
@@ -242,27 +276,55 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
       x[m] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     }
 #pragma unroll
-    for (int m = 0; m < 32; ++m) {
+    for (int m = 0; m < 16; ++m) {
       T[(o + m) * kLdA + o + j] = x[m];
       st_tp_one(tpzt, o + m, o + j, x[m], bet, eg);
     }
+  } else if (warp >= 4) {   // zeros of the upper-right 16x16 blocks inside the 32x32 diagonal blocks
+    const int t = tid - 128;             // 128 threads
+    const int blk = t >> 6, r = (t >> 2) & 15, part = t & 3;   // block, row, quarter row
+    const int rr = 32 * blk + r, c0 = 32 * blk + 16 + 4 * part;
+    *reinterpret_cast<float4*>(T + rr * kLdA + c0) = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (part < 2) {   // 16 bf16 = two 16-byte chunks per row and tile
+      const uint32_t off = sw128_off(rr, (32 * blk + 16) / 8 + part);
+      *reinterpret_cast<uint4*>(tpzt + off) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(tpzt + 24576 + off) = make_uint4(0, 0, 0, 0);
+    }
   }
   __syncthreads();
-  constexpr int kLdC = 40;    // pitch of the 32x32 scratch tile (conflict-free B fragments)
-  const int mt = warp >> 2, nt = warp & 3;
-  {  // step 2a: X = A[32:64, 0:32] T[0:32, 0:32]
+  const int g = lane >> 2, t = lane & 3;
+  if (warp < 4) {   // step 2a: X_B = A[32B+16.., 32B..] T[32B.., 32B..] (16x16, tile nt of block B)
+    const int B = warp >> 1, nt = warp & 1, o = 32 * B;
     float d[4];
-    mma_tile_3xtf32<4>(d, A + (32 + 16 * mt) * kLdA, kLdA, T + 8 * nt, kLdA, lane);
-    const int g = lane >> 2, t = lane & 3;
+    mma_tile_tf32<2>(d, A + (o + 16) * kLdA + o, kLdA, T + o * kLdA + o + 8 * nt, kLdA, lane);
+    float* Xp = X + 16 * B + 8 * nt;
+    *reinterpret_cast<float2*>(Xp + g * kLdC + 2 * t) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(Xp + (g + 8) * kLdC + 2 * t) = make_float2(d[2], d[3]);
+  }
+  __syncthreads();
+  if (warp < 4) {   // step 2b: T[32B+16.., 32B..] = T_11 X_B
+    const int B = warp >> 1, nt = warp & 1, o = 32 * B;
+    float d[4];
+    mma_tile_tf32<2>(d, T + (o + 16) * kLdA + o + 16, kLdA, X + 16 * B + 8 * nt, kLdC, lane);
+    const int row = o + 16 + g, col = o + 8 * nt + 2 * t;
+    *reinterpret_cast<float2*>(T + row * kLdA + col) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(T + (row + 8) * kLdA + col) = make_float2(d[2], d[3]);
+    st_tp_pair(tpzt, row, col, d[0], d[1], bet, eg);
+    st_tp_pair(tpzt, row + 8, col, d[2], d[3], bet, eg);
+  }
+  __syncthreads();
+  const int mt = warp >> 2, nt = warp & 3;
+  {  // step 3a: X = A[32:64, 0:32] T[0:32, 0:32]
+    float d[4];
+    mma_tile_tf32<4>(d, A + (32 + 16 * mt) * kLdA, kLdA, T + 8 * nt, kLdA, lane);
     float* Xp = X + 16 * mt * kLdC + 8 * nt;
     *reinterpret_cast<float2*>(Xp + g * kLdC + 2 * t) = make_float2(d[0], d[1]);
     *reinterpret_cast<float2*>(Xp + (g + 8) * kLdC + 2 * t) = make_float2(d[2], d[3]);
   }
   __syncthreads();
-  {  // step 2b: T[32:64, 0:32] = T[32:64, 32:64] X  (only the bf16 tiles need it)
+  {  // step 3b: T[32:64, 0:32] = T[32:64, 32:64] X  (only the bf16 tiles need it)
     float d[4];
-    mma_tile_3xtf32<4>(d, T + (32 + 16 * mt) * kLdA + 32, kLdA, X + 8 * nt, kLdC, lane);
-    const int g = lane >> 2, t = lane & 3;
+    mma_tile_tf32<4>(d, T + (32 + 16 * mt) * kLdA + 32, kLdA, X + 8 * nt, kLdC, lane);
     const int row = 32 + 16 * mt + g, col = 8 * nt + 2 * t;
     st_tp_pair(tpzt, row, col, d[0], d[1], bet, eg);
     st_tp_pair(tpzt, row + 8, col, d[2], d[3], bet, eg);
