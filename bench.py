@@ -216,17 +216,25 @@ def time_decode_e2e(K, batch, steps, warmup, flush, seed=0):
     from gdn_kernel_b200 import workloads as W
 
     x = W.make_decode_inputs(batch, seed=seed, device="cuda")
-    host_in = [t.cpu().pin_memory() for t in (x.q, x.k, x.v, x.a, x.b)]
-    dev_in = [t.clone() for t in (x.q, x.k, x.v, x.a, x.b)]
+    # The step's token inputs (q, k, v, a, b: all bf16) packed back to back in
+    # one pinned host buffer and one device buffer, so each step moves them with
+    # a single host-to-device copy; the kernel reads views of the device buffer.
+    parts = (x.q, x.k, x.v, x.a, x.b)
+    sizes = [t.numel() for t in parts]
+    host_in = torch.cat([t.reshape(-1).cpu() for t in parts]).pin_memory()
+    dev_in = torch.empty_like(host_in, device="cuda")
+    views, off = [], 0
+    for t, n in zip(parts, sizes):
+        views.append(dev_in[off:off + n].view(t.shape))
+        off += n
     out = torch.empty(batch, 1, H_V, D, dtype=torch.bfloat16, device="cuda")
     host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    h2d = host_in.numel() * host_in.element_size()
     d2h = host_out.numel() * host_out.element_size()
 
     def step():
-        for d, h in zip(dev_in, host_in):
-            d.copy_(h, non_blocking=True)
-        q, k, v, a, b = dev_in
+        dev_in.copy_(host_in, non_blocking=True)
+        q, k, v, a, b = views
         K.gdn_decode(q, k, v, x.state, x.A_log, a, x.dt_bias, b, x.scale, out, x.state)
         host_out.copy_(out, non_blocking=True)
 
@@ -522,7 +530,9 @@ def run_gpu(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "path": "gdn_kernel_b200.gdn_decode -> libgdn_b200.so gdn_b200_decode, "
-                            "pinned host q/k/v/a/b in, output out; state resident in HBM"},
+                            "q/k/v/a/b packed in one pinned host buffer (one host-to-device "
+                            "copy per step), output copied back each step; state resident in "
+                            "HBM"},
             "gpu_launches": args.steps,
             "clocks": clocks,
         }
