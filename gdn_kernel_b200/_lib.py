@@ -25,6 +25,7 @@ STATUS_TMA_TIMEOUT = 1
 STATUS_MMA_TIMEOUT = 2
 STATUS_BAD_SEQLENS = 4
 STATUS_BAD_INDEX = 8
+STATUS_SELFTEST_WAIT = 16
 
 # Every symbol the header declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -60,6 +61,7 @@ _SIGNATURES = {
     "gdn_b200_state_affine": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64, _P]),
     "gdn_b200_device_status": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32),
                                               ctypes.c_int32]),
+    "gdn_b200_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _P]),
     "gdn_b200_last_error": (ctypes.c_char_p, []),
     "gdn_b200_abi_version": (ctypes.c_int32, []),
 }

@@ -630,4 +630,33 @@ extern "C" int gdn_b200_device_status(int32_t device, uint32_t* status, int32_t 
 
 extern "C" const char* gdn_b200_last_error(void) { return t_last_error.c_str(); }
 
+// ---------------------------------------------------------------- bounded-wait self-test
+namespace gdn {
+// One warp waits on an mbarrier that nothing arrives on, with the same bounded
+// wait the prefill kernels use but a caller-chosen limit.  When the limit runs
+// out it records kStatusSelftestWait and returns, leaving the context usable.
+__global__ void gdn_selftest_wait_kernel(unsigned long long limit_ns, unsigned int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbarrier_init();
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(&bar, 0, limit_ns);
+  if (!ok && threadIdx.x == 0) atomicOr(status, kStatusSelftestWait);
+}
+}  // namespace gdn
+
+extern "C" int gdn_b200_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  t_last_error.clear();
+  if (limit_ns == 0 || limit_ns > 1000000000ull)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 1e9]");
+  unsigned int* status = nullptr;
+  if (int rc = device_setup(&status)) return rc;
+  gdn_selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "self-test launch");
+  return GDN_B200_OK;
+}
+
 extern "C" int32_t gdn_b200_abi_version(void) { return 101; }

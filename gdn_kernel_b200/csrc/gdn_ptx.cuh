@@ -20,6 +20,7 @@ enum : unsigned int {
   kStatusTmaTimeout = 1u,
   kStatusMmaTimeout = 2u,
   kStatusBadSeqlens = 4u,   // cu_seqlens entry outside [0, total_tokens]
+  kStatusSelftestWait = 16u,   // the wait of the bounded-wait self-test ran out
 };
 
 // Upper bound on any spin on an mbarrier, in nanoseconds of %globaltimer.
@@ -83,12 +84,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Bounded wait on the given phase parity.  Returns false when the limit ran
 // out; the caller records an error status and leaves its loop.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 

@@ -42,6 +42,7 @@ extern "C" {
 #define GDN_B200_STATUS_MMA_TIMEOUT 2u   /* a prefill tensor-core wait exceeded its bound */
 #define GDN_B200_STATUS_BAD_SEQLENS 4u   /* a cu_seqlens entry was outside [0, total_tokens] */
 #define GDN_B200_STATUS_BAD_INDEX 8u     /* a state-pool index was >= pool_size */
+#define GDN_B200_STATUS_SELFTEST_WAIT 16u /* gdn_b200_selftest_wait_timeout's wait ran out */
 
 /*
  * One T=1 decode step for `batch` sequences.
@@ -206,6 +207,15 @@ int gdn_b200_prefill_static(const void* q, const void* k, const void* v, const f
  * in the reference, which performs no device-side checks.
  */
 int gdn_b200_device_status(int32_t device, uint32_t* status, int32_t clear);
+
+/*
+ * Diagnostic of the device-side failure detection: launches one warp that waits
+ * on an mbarrier nothing ever arrives on, with the bounded wait the prefill
+ * kernels use but a limit of `limit_ns` nanoseconds (at most 1 s).  The wait
+ * runs out, the kernel sets GDN_B200_STATUS_SELFTEST_WAIT and returns; the
+ * context stays usable.  No counterpart in the reference.
+ */
+int gdn_b200_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
 /* Message of the last failing call on this thread ("" if none). */
 const char* gdn_b200_last_error(void);

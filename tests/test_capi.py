@@ -109,3 +109,11 @@ def test_decode_pool_rejects_bad_arguments():
     assert call() == _lib.GDN_B200_ERR_INVALID_ARGUMENT            # null pointers
     assert b"null" in lib.gdn_b200_last_error()
     assert call(batch=0) == _lib.GDN_B200_OK                         # nothing to do
+
+
+def test_selftest_wait_rejects_bad_limits():
+    lib = _lib.load()
+    z = ctypes.c_void_p(0)
+    assert lib.gdn_b200_selftest_wait_timeout(0, z) == _lib.GDN_B200_ERR_INVALID_ARGUMENT
+    assert lib.gdn_b200_selftest_wait_timeout(5_000_000_000, z) == \
+        _lib.GDN_B200_ERR_INVALID_ARGUMENT

@@ -96,7 +96,7 @@ def _emulate(x, world):
     return torch.cat(outs), end
 
 
-@pytest.mark.parametrize("T,world", [(4096, 2), (8192, 4), (1000, 3)])
+@pytest.mark.parametrize("T,world", [(4096, 2), (8192, 4), (1000, 3), (100, 3)])
 def test_cp_emulated_matches_whole_sequence(T, world):
     x = W.make_prefill_inputs([T], seed=200 + world, device="cuda")
     out, end = _emulate(x, world)

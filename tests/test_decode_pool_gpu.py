@@ -75,7 +75,7 @@ def test_t1_permuted_slots_padding_and_write_slots(idx_dtype):
         assert torch.equal(pool[s], x.pool[s])
 
 
-@pytest.mark.parametrize("T", [2, 4, 7])
+@pytest.mark.parametrize("T", [2, 4, 7, 20])   # 20: two staged token groups of 16
 def test_mtp_fp32_with_intermediate_states(T):
     x = W.make_pool_decode_inputs(6, T, 9, seed=10 + T)
     out, pool, inter = _run(x, x.indices, inter=True)
@@ -85,7 +85,7 @@ def test_mtp_fp32_with_intermediate_states(T):
     torch.testing.assert_close(inter, ri, **DECODE_STATE_TOL)
 
 
-@pytest.mark.parametrize("T", [1, 3])
+@pytest.mark.parametrize("T", [1, 3, 17])
 def test_bf16_state_pool(T):
     x = W.make_pool_decode_inputs(4, T, 6, seed=30 + T, state_dtype=torch.bfloat16)
     out, pool, inter = _run(x, x.indices, inter=True)
