@@ -58,8 +58,9 @@ constexpr int kLdA = 68;                           // fp32 row pitch of A and T 
 constexpr uint32_t kOffAF = kOffVND + 16384;       // fp32 A [64][68]
 constexpr uint32_t kOffTF = kOffAF + 64 * kLdA * 4;  // fp32 T [64][68]
 constexpr uint32_t kOffXS = kOffTF + 64 * kLdA * 4;  // fp32 scratch of the solve, 32x40
-constexpr uint32_t kOffGate = kOffXS + 32 * 40 * 4;  // 2 buffers x {gamma, beta, e^gamma}[64]
-constexpr uint32_t kOffBar = kOffGate + 2 * 3 * 256; // 5 mbarriers
+constexpr uint32_t kGateFloats = 4 * 64;             // {gamma, beta, e^gamma, F}[64], F below
+constexpr uint32_t kOffGate = kOffXS + 32 * 40 * 4;  // 2 gate buffers
+constexpr uint32_t kOffBar = kOffGate + 2 * kGateFloats * 4;  // 5 mbarriers
 constexpr uint32_t kOffTmemPtr = kOffBar + 48;
 constexpr uint32_t kSmemUsed = kOffTmemPtr + 16;
 constexpr uint32_t kPrefillSmem = kSmemUsed + 1024;  // slack to align the base
@@ -331,45 +332,79 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
   }
 }
 
+// Decay factors e^{gamma_i - gamma_j} of one row i over the 32 columns
+// j = jb .. jb+31, zero where j > i or i >= clen.  gamma is non-increasing,
+// so every factor is at most 1; each one is formed as a product of two
+// factors that are also at most 1, through the end r = (j | 7) of j's
+// 8-column sub-block when r <= i:
+//   e^{gamma_i - gamma_j} = e^{gamma_i - gamma_r} * F[j],  F[j] = e^{gamma_r - gamma_j}
+// (F per chunk from gate_finish).  Only the sub-block holding i itself needs
+// direct exponentials.  Neither factor can overflow, and if one underflowed
+// the exact product would too.  That is 11 exponentials per row in a
+// diagonal 32x32 block and 4 in the block below it, instead of 32.
+__device__ __forceinline__ void decay_row(int i, int jb, int clen, const float* gam,
+                                          const float* fsub, float* f) {
+  const float gi = gam[i];
+  const int d = i - jb;   // >= 0 (the caller skips blocks above the diagonal)
+  if (d >= 32) {          // the whole block lies below row i
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const float sb = __expf(gi - gam[jb + 8 * b + 7]);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) f[8 * b + jj] = sb * fsub[jb + 8 * b + jj];
+    }
+  } else {                // diagonal block: i's own sub-block is sb, its offset in it dj
+    const int sb = d >> 3, dj = d & 7;
+    float e8[8];
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) e8[jj] = __expf(gi - gam[jb + 8 * sb + jj]);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const float s_b = b < 3 ? __expf(gi - gam[jb + 8 * b + 7]) : 0.f;   // used when b < sb
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj)
+        f[8 * b + jj] = b < sb ? s_b * fsub[jb + 8 * b + jj] : (b == sb && jj <= dj ? e8[jj] : 0.f);
+    }
+  }
+  if (i >= clen) {
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) f[jj] = 0.f;
+  }
+}
+
 // P (rows 0-63 of D_QK) to the bf16 P tile and A (rows 64-127) to fp32, for
 // the TMEM lane `row` of this thread and the 32 columns of its `half`:
 //   P_ij = (QK^T)_ij e^{gamma_i - gamma_j}          (j <= i < clen, else 0)
 //   A_ij = -beta_i (KK^T)_ij e^{gamma_i - gamma_j}  (j < i < clen, else 0)
 // A 32-column tile that lies wholly above the diagonal skips the exponentials.
 __device__ __forceinline__ void pa_epilogue(uint32_t tm_qk, int row, int half, int quad, int clen,
-                                            const float* gam, const float* bet, uint8_t* ptile,
-                                            float* AF) {
+                                            const float* gam, const float* bet, const float* fsub,
+                                            uint8_t* ptile, float* AF) {
   const int i = row & 63;
   const bool upper = half == 1 && (quad & 1) == 0;   // rows 0-31 x cols 32-63
+  if (upper) {
+    if (row < 64) zero_half_row(ptile, i, 4);
+    return;
+  }
+  float r[32], f[32];
+  tmem_ld32(tm_qk + 32 * half, r);
+  decay_row(i, 32 * half, clen, gam, fsub, f);   // overlaps the TMEM load
+  tmem_wait_ld();
   if (row < 64) {
-    if (upper) {
-      zero_half_row(ptile, i, 4);
-    } else {
-      float r[32];
-      tmem_ld32(tm_qk + 32 * half, r);
-      tmem_wait_ld();
-      const float gi = gam[i];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = 32 * half + jj;
-        r[jj] = (j <= i && i < clen) ? r[jj] * __expf(gi - gam[j]) : 0.f;
-      }
-      st_half_row_bf16(ptile, i, 4 * half, r, 1.0f);
-    }
-  } else if (!upper) {
-    float r[32];
-    tmem_ld32(tm_qk + 32 * half, r);
-    tmem_wait_ld();
-    const float gi = gam[i], nb = -bet[i];
+    for (int jj = 0; jj < 32; ++jj) r[jj] *= f[jj];
+    st_half_row_bf16(ptile, i, 4 * half, r, 1.0f);
+  } else {
+    const float nb = -bet[i];
     float* arow = AF + i * kLdA + 32 * half;
 #pragma unroll
     for (int jj = 0; jj < 32; jj += 4) {
       float4 o;
       const int j = 32 * half + jj;
-      o.x = (j + 0 < i && i < clen) ? nb * r[jj + 0] * __expf(gi - gam[j + 0]) : 0.f;
-      o.y = (j + 1 < i && i < clen) ? nb * r[jj + 1] * __expf(gi - gam[j + 1]) : 0.f;
-      o.z = (j + 2 < i && i < clen) ? nb * r[jj + 2] * __expf(gi - gam[j + 2]) : 0.f;
-      o.w = (j + 3 < i && i < clen) ? nb * r[jj + 3] * __expf(gi - gam[j + 3]) : 0.f;
+      o.x = j + 0 < i ? nb * r[jj + 0] * f[jj + 0] : 0.f;
+      o.y = j + 1 < i ? nb * r[jj + 1] * f[jj + 1] : 0.f;
+      o.z = j + 2 < i ? nb * r[jj + 2] * f[jj + 2] : 0.f;
+      o.w = j + 3 < i ? nb * r[jj + 3] * f[jj + 3] : 0.f;
       *reinterpret_cast<float4*>(arow + jj) = o;
     }
   }
@@ -412,7 +447,9 @@ __device__ __forceinline__ void qprime_row(uint8_t* tile, int c, float e, const 
 
 // Gates of one chunk (one warp, two positions per lane).  gate_inputs loads
 // a and b (issued early, so their latency hides behind other work);
-// gate_finish forms log g, its inclusive prefix sum gamma, e^gamma and beta.
+// gate_finish forms log g, its inclusive prefix sum gamma, e^gamma, beta and
+// F[j] = e^{gamma_{j|7} - gamma_j} (the decay from j to the end of its
+// 8-position sub-block, used by decay_row).
 // Positions past the sequence end get log g = 0 and beta = 0.
 struct GateIn {
   float a[2], b[2];
@@ -438,7 +475,7 @@ __device__ __forceinline__ GateIn gate_inputs(const PrefillParams& p, long long 
 }
 
 __device__ __forceinline__ void gate_finish(const GateIn& g, float A_neg, float dtb, int lane,
-                                            float* gam, float* bet, float* eg) {
+                                            float* gam, float* bet, float* eg, float* fsub) {
   float lg[2], bt[2];
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
@@ -456,6 +493,10 @@ __device__ __forceinline__ void gate_finish(const GateIn& g, float A_neg, float 
   gam[2 * lane + 1] = g1;
   eg[2 * lane] = expf(g0);
   eg[2 * lane + 1] = expf(g1);
+  // position 2 lane | 7 ends this lane's sub-block; lane (lane | 3) holds it as g1
+  const float gend = __shfl_sync(0xffffffffu, g1, lane | 3);
+  fsub[2 * lane] = expf(gend - g0);
+  fsub[2 * lane + 1] = expf(gend - g1);
   bet[2 * lane] = bt[0];
   bet[2 * lane + 1] = bt[1];
 }
@@ -554,7 +595,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   if (warp == 1) {
     const GateIn g0 = gate_inputs(p, s0, static_cast<int>(min(static_cast<long long>(kChunk), len)),
                                   head, lane);
-    gate_finish(g0, A_neg, dtb, lane, gate_base, gate_base + 64, gate_base + 128);
+    gate_finish(g0, A_neg, dtb, lane, gate_base, gate_base + 64, gate_base + 128, gate_base + 192);
   }
 
   // Initial state: thread (k = row, half) holds S^T[k][64*half + j] = S[64*half + j][k].
@@ -611,7 +652,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const int clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - cstart));
     const bool has_next = ci + 1 < nchunks;
     const long long nstart = cstart + kChunk;
-    const float* gam = gate_base + (ci & 1) * 192;
+    const float* gam = gate_base + (ci & 1) * kGateFloats;
     const float* bet = gam + 64;
     const float* eg = gam + 128;
 
@@ -654,7 +695,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     mma_done();
 
     // ---- 3. P (rows 0-63) to bf16, A (rows 64-127) to fp32.
-    pa_epilogue(tmem + tm_lane + kTmQK, row, half, quad, clen, gam, bet, smem + kOffTPZT + 8192, AF);
+    pa_epilogue(tmem + tm_lane + kTmQK, row, half, quad, clen, gam, bet, gam + 192,
+                smem + kOffTPZT + 8192, AF);
     tc_fence_before();
     __syncthreads();
 
@@ -729,8 +771,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       st_half_row_bf16(smem + kOffVND + half * 8192, c, 0, r, dec);
       st_half_row_bf16(smem + kOffVND + half * 8192, c, 4, r + 32, dec);
     } else if (warp == 1 && has_next) {
-      float* ng = gate_base + ((ci + 1) & 1) * 192;
-      gate_finish(next_gates, A_neg, dtb, lane, ng, ng + 64, ng + 128);
+      float* ng = gate_base + ((ci + 1) & 1) * kGateFloats;
+      gate_finish(next_gates, A_neg, dtb, lane, ng, ng + 64, ng + 128, ng + 192);
     }
     fence_proxy_async_smem();
     tc_fence_before();

@@ -187,8 +187,8 @@ constexpr uint32_t kP1OffR1 = kP1OffTPZT + 32768;
 constexpr uint32_t kP1TbOff = 24576;                   // T_b within TPZT
 constexpr uint32_t kP1OffTFinR = 64 * kLdA * 4;        // T after A within a scratch region
 constexpr uint32_t kP1OffXS = kP1OffR1 + kP1Region;
-constexpr uint32_t kP1OffGate = kP1OffXS + 32 * 40 * 4;   // 2 x (gamma, beta, e^gamma [64])
-constexpr uint32_t kP1OffBar = kP1OffGate + 2 * 768;      // TMA [2], MMA
+constexpr uint32_t kP1OffGate = kP1OffXS + 32 * 40 * 4;   // 2 gate buffers (gate_finish)
+constexpr uint32_t kP1OffBar = kP1OffGate + 2 * kGateFloats * 4;   // TMA [2], MMA
 constexpr uint32_t kP1OffTmemPtr = kP1OffBar + 32;
 constexpr uint32_t kP1Smem = kP1OffTmemPtr + 16 + 1024;
 constexpr uint32_t kP1TmQK = 0;       // 64 columns
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   const PrefillParams& p = sp.base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2, row = quad * 32 + lane;
-  const long long n_items = static_cast<long long>(sp.header[0]) * p.h_v;
+  const int n_chunks = sp.header[0];
 
   uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + kP1OffBar);   // [2]
   uint64_t* bar_mma = bar_tma + 2;
@@ -215,7 +215,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   float* XS = reinterpret_cast<float*>(smem + kP1OffXS);
   uint8_t* tpzt = smem + kP1OffTPZT;
   auto region = [&](int r) { return smem + (r ? kP1OffR1 : kP1OffR0); };
-  auto gates = [&](int r) { return reinterpret_cast<float*>(smem + kP1OffGate + 768 * r); };
+  auto gates = [&](int r) {
+    return reinterpret_cast<float*>(smem + kP1OffGate + kGateFloats * 4 * r);
+  };
 
   if (warp == 0) {
     tmem_alloc(tmem_ptr, kP1TmCols);
@@ -243,12 +245,28 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   const uint32_t tm_lane = static_cast<uint32_t>(quad * 32) << 16;
   const uint32_t a_tpzt = smem_u32(tpzt);
 
-  // Item `it`'s Q/K tiles into region r (thread 0); its gate inputs into warp
-  // 1's registers (finished into gate buffer r later, once they have landed).
-  auto issue_item = [&](long long it, const ChunkInfo& info, int r, GateIn& gi) {
-    const int head = static_cast<int>(it % p.h_v);
+  // Items are (chunk, v-head) pairs in chunk-major order; a CTA steps through
+  // them gridDim.x at a time, i.e. by (dc chunks, dh heads), without dividing.
+  struct Item {
+    int c, h;
+  };
+  const int dc = static_cast<int>(gridDim.x) / p.h_v, dh = static_cast<int>(gridDim.x) % p.h_v;
+  auto advance = [&](Item x) {
+    x.c += dc;
+    x.h += dh;
+    if (x.h >= p.h_v) {
+      x.h -= p.h_v;
+      ++x.c;
+    }
+    return x;
+  };
+  auto table_at = [&](const Item& x) {
+    return x.c < n_chunks ? sp.table[x.c] : ChunkInfo{-1, 0, 0};
+  };
+  // An item's Q/K tiles into region r (thread 0).
+  auto issue_tiles = [&](const Item& x, const ChunkInfo& info, int r) {
     if (tid == 0) {
-      const int hq = head / (p.h_v / p.h_qk);
+      const int hq = x.h / (p.h_v / p.h_qk);
       const int t0 = static_cast<int>(info.cstart);
       mbar_arrive_expect_tx(bar_tma + r, 4 * kTileBytes);
 #pragma unroll
@@ -257,17 +275,22 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
         tma_load_3d(region(r) + kb * 16384 + 8192, &tm_k, bar_tma + r, kb * 64, hq, t0);
       }
     }
-    if (warp == 1) gi = gate_inputs(p, info.cstart, info.clen, head, lane);
   };
-  auto finish_gates = [&](long long it, const GateIn& gi, int r) {
+  // An item's gate inputs into warp 1's registers, issued a whole item before
+  // gate_finish needs them (a, b and the head's A_log, dt_bias).
+  float g_alog = 0.f, g_dtb = 0.f;
+  auto load_gates = [&](const Item& x, const ChunkInfo& info, GateIn& gi) {
     if (warp == 1) {
-      const int head = static_cast<int>(it % p.h_v);
-      float* g = gates(r);
-      gate_finish(gi, -expf(p.A_log[head]), p.dt_bias[head], lane, g, g + 64, g + 128);
+      gi = gate_inputs(p, info.cstart, info.clen, x.h, lane);
+      g_alog = p.A_log[x.h];
+      g_dtb = p.dt_bias[x.h];
     }
   };
-  auto table_at = [&](long long it) {
-    return it < n_items ? sp.table[static_cast<int>(it / p.h_v)] : ChunkInfo{-1, 0, 0};
+  auto finish_gates = [&](const GateIn& gi, int r) {
+    if (warp == 1) {
+      float* g = gates(r);
+      gate_finish(gi, -expf(g_alog), g_dtb, lane, g, g + 64, g + 128, g + 192);
+    }
   };
 
   unsigned int code = 0;
@@ -275,21 +298,26 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   bool failed = false;
   int pend_r = -1;            // region whose copy is in flight and not yet waited for
   uint32_t pend_parity = 0;
-  long long it = blockIdx.x;
-  ChunkInfo cur = table_at(it);
+  Item cur{static_cast<int>(blockIdx.x) / p.h_v, static_cast<int>(blockIdx.x) % p.h_v};
+  Item nxt = advance(cur);
+  ChunkInfo cur_info = table_at(cur);
+  ChunkInfo nxt_info = table_at(nxt);
   GateIn gi{};
-  if (it < n_items) {
-    issue_item(it, cur, 0, gi);
+  if (cur.c < n_chunks) {
+    issue_tiles(cur, cur_info, 0);
     pend_r = 0;
     pend_parity = 0;
-    finish_gates(it, gi, 0);
+    load_gates(cur, cur_info, gi);
+    finish_gates(gi, 0);
   }
-  for (int j = 0; it < n_items; ++j, it += gridDim.x) {
+  for (int j = 0; cur.c < n_chunks; ++j) {
     const int r = j & 1;
-    const int gc = static_cast<int>(it / p.h_v), head = static_cast<int>(it % p.h_v);
-    const long long nxt = it + gridDim.x;
-    const ChunkInfo nxt_info = table_at(nxt);   // its latency hides behind this item
-    const int clen = cur.clen;
+    const int gc = cur.c, head = cur.h;
+    const bool has_nxt = nxt.c < n_chunks;
+    const Item nx2 = advance(nxt);
+    const ChunkInfo nx2_info = table_at(nx2);   // used an item from now
+    if (has_nxt) load_gates(nxt, nxt_info, gi);
+    const int clen = cur_info.clen;
     uint8_t* qkw = region(r);
     float* AF = reinterpret_cast<float*>(region(r ^ 1));
     float* TF = reinterpret_cast<float*>(region(r ^ 1) + kP1OffTFinR);
@@ -337,7 +365,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     if (!ok) code |= kStatusMmaTimeout;
     if (__syncthreads_or(!ok)) { failed = true; break; }
     tc_fence_after();
-    pa_epilogue(tmem + tm_lane + kP1TmQK, row, half, quad, clen, gam, bet, tpzt + 8192, AF);
+    pa_epilogue(tmem + tm_lane + kP1TmQK, row, half, quad, clen, gam, bet, gam + 192, tpzt + 8192,
+                AF);
     tc_fence_before();
     __syncthreads();
     solve_unit_lower(AF, TF, XS, tpzt, bet, eg, tid);
@@ -345,8 +374,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     tc_fence_before();
     __syncthreads();
     // The solve's scratch is dead: the next item's tiles go there now.
-    if (nxt < n_items) {
-      issue_item(nxt, nxt_info, r ^ 1, gi);
+    if (has_nxt) {
+      issue_tiles(nxt, nxt_info, r ^ 1);
       pend_r = r ^ 1;
       pend_parity = ((j + 1) >> 1) & 1;
     }
@@ -407,7 +436,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     }
     // The next item's gates (its loads have landed by now) into the other buffer;
     // that buffer's previous contents (item j - 1's gamma) were drained above.
-    if (nxt < n_items) finish_gates(nxt, gi, r ^ 1);
+    if (has_nxt) finish_gates(gi, r ^ 1);
     fence_proxy_async_smem();
     tc_fence_before();
     if (__syncthreads_or(!ok)) { failed = true; break; }
@@ -422,7 +451,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
       bulk_store(rec + kRecOffGam, gam, 256);
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
-    cur = nxt_info;
+    cur = nxt;
+    cur_info = nxt_info;
+    nxt = nx2;
+    nxt_info = nx2_info;
   }
   // Everything in flight lands before the CTA's shared memory and TMEM go
   // away: bulk stores (thread 0's groups), and on a failed run the copy still
