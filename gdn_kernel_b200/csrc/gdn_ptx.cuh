@@ -120,6 +120,15 @@ __device__ __forceinline__ int mbar_wait_or_abort(uint64_t* bar, uint32_t parity
 
 // One lane of a converged warp (elect.sync); tcgen05.mma and commit are
 // issued by that lane.
+// Named barriers (ids 1-15; 0 is __syncthreads): `count` threads, whole warps.
+// named_arrive signals without waiting; named_sync signals and waits.
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred;
   asm volatile(

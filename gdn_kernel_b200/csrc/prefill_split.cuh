@@ -188,14 +188,17 @@ constexpr uint32_t kP1TbOff = 24576;                   // T_b within TPZT
 constexpr uint32_t kP1OffTFinR = 64 * kLdA * 4;        // T after A within a scratch region
 constexpr uint32_t kP1OffXS = kP1OffR1 + kP1Region;
 constexpr uint32_t kP1OffGate = kP1OffXS + 32 * 40 * 4;   // 2 gate buffers (gate_finish)
-constexpr uint32_t kP1OffBar = kP1OffGate + 2 * kGateFloats * 4;   // TMA [2], MMA
-constexpr uint32_t kP1OffTmemPtr = kP1OffBar + 32;
+constexpr uint32_t kP1OffBar = kP1OffGate + 2 * kGateFloats * 4;   // TMA [2], QK, X, W
+constexpr uint32_t kP1OffTmemPtr = kP1OffBar + 48;
 constexpr uint32_t kP1Smem = kP1OffTmemPtr + 16 + 1024;
 constexpr uint32_t kP1TmQK = 0;       // 64 columns
 constexpr uint32_t kP1TmX = 0;        // 128 columns (D_QK is consumed by then)
 constexpr uint32_t kP1TmW = 128;      // 128 columns
 constexpr uint32_t kP1TmCols = 256;
 static_assert(2 * kP1OffTFinR <= kP1Region, "A and T scratch must fit a region");
+constexpr int kP1StoreTid = kPrefillThreads - 32;       // lane 0 of the last warp: record stores
+constexpr int kP1BarPT = 1;    // named barrier: P T' tile written (warps 0-1)
+constexpr int kP1BarRec = 2;   // named barrier: an item's record tiles complete (store warp waits)
 static_assert(kP1Smem + 1024 <= 232448 / 2, "two prep CTAs must fit an SM");
 
 __global__ void __launch_bounds__(kPrefillThreads, 2)
@@ -209,8 +212,15 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   const int quad = warp & 3, half = warp >> 2, row = quad * 32 + lane;
   const int n_chunks = sp.header[0];
 
+  // One mbarrier per product, each completing once per item (phase parity =
+  // item parity j & 1).  Warps wait on them without a CTA-wide barrier in
+  // between, so a shared barrier could be a whole phase ahead of a slow warp
+  // and alias its parity; with one per product, the item's first CTA-wide
+  // barrier keeps every warp within one phase.
   uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + kP1OffBar);   // [2]
-  uint64_t* bar_mma = bar_tma + 2;
+  uint64_t* bar_qk = bar_tma + 2;
+  uint64_t* bar_x = bar_tma + 3;
+  uint64_t* bar_w = bar_tma + 4;
   uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + kP1OffTmemPtr);
   float* XS = reinterpret_cast<float*>(smem + kP1OffXS);
   uint8_t* tpzt = smem + kP1OffTPZT;
@@ -226,7 +236,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   if (tid == 32) {
     mbar_init(bar_tma, 1);
     mbar_init(bar_tma + 1, 1);
-    mbar_init(bar_mma, 1);
+    mbar_init(bar_qk, 1);
+    mbar_init(bar_x, 1);
+    mbar_init(bar_w, 1);
     fence_mbarrier_init();
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
@@ -263,9 +275,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   auto table_at = [&](const Item& x) {
     return x.c < n_chunks ? sp.table[x.c] : ChunkInfo{-1, 0, 0};
   };
-  // An item's Q/K tiles into region r (thread 0).
+  // An item's Q/K tiles into region r (the store thread, off warp 0's path).
   auto issue_tiles = [&](const Item& x, const ChunkInfo& info, int r) {
-    if (tid == 0) {
+    if (tid == kP1StoreTid) {
       const int hq = x.h / (p.h_v / p.h_qk);
       const int t0 = static_cast<int>(info.cstart);
       mbar_arrive_expect_tx(bar_tma + r, 4 * kTileBytes);
@@ -294,7 +306,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   };
 
   unsigned int code = 0;
-  uint32_t mma_phase = 0;
+  int w_issued = 0;           // W commits so far (the drain's commit follows them)
   bool failed = false;
   int pend_r = -1;            // region whose copy is in flight and not yet waited for
   uint32_t pend_parity = 0;
@@ -329,23 +341,25 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     bool ok = mbar_wait(bar_tma + r, (j >> 1) & 1);
     if (ok) pend_r = -1;
     else code |= kStatusTmaTimeout;
-    if (clen < kChunk) {   // rows past the sequence end: zero Q and K rows
-      const int nrow = kChunk - clen;
-      for (int e = tid; e < 4 * nrow * 8; e += kPrefillThreads) {
-        const int reg = e / (nrow * 8);
-        const int rr = clen + (e / 8) % nrow;
-        *reinterpret_cast<uint4*>(qkw + (reg >> 1) * 16384 + (reg & 1) * 8192 +
-                                  sw128_off(rr, e & 7)) = make_uint4(0, 0, 0, 0);
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    if (__syncthreads_or(!ok)) { failed = true; break; }   // also publishes the gates
-    tc_fence_after();
 
-    // D_QK = [Q ; K] K^T, with K (rows 64-127 of the stacked tile) as the B operand.
+    // D_QK = [Q ; K] K^T, with K (rows 64-127 of the stacked tile) as the B
+    // operand, issued by warp 0 as soon as the tiles have landed: no CTA-wide
+    // barrier first (this item's gates were published by the previous item's
+    // last one, and the same warp zeroes the rows past a short chunk's end).
     if (warp == 0) {
-      if (elect_one()) {
+      if (ok && clen < kChunk) {
+        const int nrow = kChunk - clen;
+        for (int e = lane; e < 4 * nrow * 8; e += 32) {
+          const int reg = e / (nrow * 8);
+          const int rr = clen + (e / 8) % nrow;
+          *reinterpret_cast<uint4*>(qkw + (reg >> 1) * 16384 + (reg & 1) * 8192 +
+                                    sw128_off(rr, e & 7)) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      tc_fence_after();
+      if (ok && elect_one()) {
         const uint32_t idesc = idesc_bf16_f32(128, 64, 0, 0);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
@@ -353,17 +367,19 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
           umma_bf16(tmem + kP1TmQK, sdesc_sw128(a_qkw + koff, 16, 1024),
                     sdesc_sw128(a_qkw + 8192 + koff, 16, 1024), idesc, s > 0 ? 1u : 0u);
         }
-        umma_commit(bar_mma);
+        umma_commit(bar_qk);
       }
       __syncwarp();
     }
     // The previous item's records must have been read out of TPZT and the
     // other region (its [Q;K] tile) before the P/A epilogue overwrites them.
-    if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-    ok = mbar_wait(bar_mma, mma_phase & 1);
-    ++mma_phase;
-    if (!ok) code |= kStatusMmaTimeout;
-    if (__syncthreads_or(!ok)) { failed = true; break; }
+    if (tid == kP1StoreTid) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    if (ok) {
+      ok = mbar_wait(bar_qk, j & 1);
+      if (!ok) code |= kStatusMmaTimeout;
+    }
+    // (also the first CTA-wide barrier after a failure in the previous item)
+    if (__syncthreads_or(!ok || code != 0)) { failed = true; break; }
     tc_fence_after();
     pa_epilogue(tmem + tm_lane + kP1TmQK, row, half, quad, clen, gam, bet, gam + 192, tpzt + 8192,
                 AF);
@@ -390,23 +406,25 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
         for (int s = 0; s < 4; ++s)
           umma_bf16(tmem + kP1TmX, sdesc_sw128(a_tpzt + 8192 + s * 32, 16, 1024),
                     sdesc_sw128(a_tpzt + s * 2048, kP1TbOff, 1024), idesc, s > 0 ? 1u : 0u);
-        umma_commit(bar_mma);
+        umma_commit(bar_x);
       }
       __syncwarp();
     }
     if (quad < 2) {   // half 0: P T' over P (A rows 64-127 of D_W); half 1: P' to the scratch rows
-      if (!mbar_wait(bar_mma, mma_phase & 1)) code |= kStatusMmaTimeout;
+      if (!mbar_wait(bar_x, j & 1)) code |= kStatusMmaTimeout;
       tc_fence_after();
       float rr[64];
       tmem_ld64(tmem + tm_lane + kP1TmX + 64 * half, rr);
       st_row_bf16(tpzt + (half == 0 ? 8192 : 16384), row, rr);
     }
-    ++mma_phase;
     fence_proxy_async_smem();
-    tc_fence_before();
-    if (__syncthreads_or(code != 0)) { failed = true; break; }
     // D_W = [T' ; P T'] K, K the MN-major B operand (64-column blocks 16 KiB
-    // apart): rows 0-63 W = T'K, rows 64-127 P W.
+    // apart): rows 0-63 W = T'K, rows 64-127 P W.  Its A operand needs P T'
+    // from warps 0 and 1 only (P' from warps 4 and 5 leaves with the records).
+    if (warp < 2) {
+      tc_fence_before();
+      named_sync(kP1BarPT, 64);
+    }
     if (warp == 0) {
       tc_fence_after();
       if (elect_one()) {
@@ -415,12 +433,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
         for (int s = 0; s < 4; ++s)
           umma_bf16(tmem + kP1TmW, sdesc_sw128(a_tpzt + s * 32, 16, 1024),
                     sdesc_sw128(a_qkw + 8192 + s * 2048, 16384, 1024), idesc, s > 0 ? 1u : 0u);
-        umma_commit(bar_mma);
+        umma_commit(bar_w);
       }
       __syncwarp();
     }
-    ok = mbar_wait(bar_mma, mma_phase & 1);
-    ++mma_phase;
+    ++w_issued;
+    ok = mbar_wait(bar_w, j & 1);
     if (!ok) code |= kStatusMmaTimeout;
     tc_fence_after();
     if (ok) {
@@ -439,11 +457,15 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     if (has_nxt) finish_gates(gi, r ^ 1);
     fence_proxy_async_smem();
     tc_fence_before();
-    if (__syncthreads_or(!ok)) { failed = true; break; }
-    tc_fence_after();
+    // Only the store thread's warp waits for the finished tiles; the others
+    // go on to the next item (its first CTA-wide barrier catches failures).
+    if (tid >= kP1StoreTid) named_sync(kP1BarRec, kPrefillThreads);
+    else named_arrive(kP1BarRec, kPrefillThreads);
     // Tile images out by bulk copies ([Q' ; -W], P', T_b, gamma); drained by
     // the next item (or the end of the kernel) before their sources change.
-    if (tid == 0) {
+    // A thread of the last warp issues them, off warp 0's path to the next
+    // item's first product.
+    if (tid == kP1StoreTid) {
       uint8_t* rec = sp.records + (static_cast<size_t>(gc) * p.h_v + head) * kRecBytes;
       bulk_store(rec + kRecOffQW, qkw, 32768);
       bulk_store(rec + kRecOffP, tpzt + 16384, 8192);
@@ -457,16 +479,17 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     nxt_info = nx2_info;
   }
   // Everything in flight lands before the CTA's shared memory and TMEM go
-  // away: bulk stores (thread 0's groups), and on a failed run the copy still
-  // pending and the tensor-core ops (one more bounded wait each).
-  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  // away: bulk stores (the store thread's groups), and on a failed run the
+  // copy still pending and the tensor-core ops (one more bounded wait each).
+  if (tid == kP1StoreTid) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  failed = failed || code != 0;
   if (failed) {
     if (pend_r >= 0) mbar_wait(bar_tma + pend_r, pend_parity);
     if (warp == 0) {
-      if (elect_one()) umma_commit(bar_mma);
+      if (elect_one()) umma_commit(bar_w);
       __syncwarp();
     }
-    mbar_wait(bar_mma, mma_phase & 1);
+    mbar_wait(bar_w, w_issued & 1);
   }
   if (code) atomicOr(p.status, code);
   tc_fence_before();
