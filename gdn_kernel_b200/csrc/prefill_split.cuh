@@ -75,7 +75,23 @@ struct SplitParams {
   uint8_t* records;       // [max_chunks][H_v] x kRecBytes
   int num_seqs;
   int max_chunks;
+  // Chunk window [c_lo, c_hi): the prep kernel does the items of table chunks
+  // in it, the chain kernel the chunks of each sequence in it (index within
+  // the sequence).  The whole call is [0, INT_MAX); a one-sequence call split
+  // into pieces runs one window per piece (chunk c of the only sequence is
+  // table chunk c).
+  int c_lo, c_hi;
 };
+
+// Programmatic dependent launch.  launch_dependents lets the grid launched
+// after this one with programmatic stream serialization start once every CTA
+// of this grid has issued it (or exited); wait blocks until the grid this one
+// was launched after has completed and its memory is visible.  Both do nothing
+// for a grid launched without that attribute / without such a dependent.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------- chunk table
 constexpr int kTableThreads = 1024;
@@ -210,7 +226,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   const PrefillParams& p = sp.base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2, row = quad * 32 + lane;
-  const int n_chunks = sp.header[0];
+  const int n_chunks = min(sp.header[0], sp.c_hi);
 
   // One mbarrier per product, each completing once per item (phase parity =
   // item parity j & 1).  Warps wait on them without a CTA-wide barrier in
@@ -310,7 +326,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   bool failed = false;
   int pend_r = -1;            // region whose copy is in flight and not yet waited for
   uint32_t pend_parity = 0;
-  Item cur{static_cast<int>(blockIdx.x) / p.h_v, static_cast<int>(blockIdx.x) % p.h_v};
+  Item cur{sp.c_lo + static_cast<int>(blockIdx.x) / p.h_v, static_cast<int>(blockIdx.x) % p.h_v};
   Item nxt = advance(cur);
   ChunkInfo cur_info = table_at(cur);
   ChunkInfo nxt_info = table_at(nxt);
@@ -496,6 +512,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, kP1TmCols);
+  // When this grid was launched to overlap the chain kernel before it (a
+  // one-sequence call in pieces), it completes only after that kernel: the
+  // next piece's chain, launched after this grid, then starts from a finished
+  // state.
+  pdl_wait();
 }
 
 // ---------------------------------------------------------------- chain kernel
@@ -562,8 +583,12 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   const int head = blockIdx.x >> 1, vs = blockIdx.x & 1, seq = blockIdx.y;
   const int hq = head / (p.h_v / p.h_qk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gc0 = sp.seq_off[seq];
-  const int nch = sp.seq_off[seq + 1] - gc0;
+  pdl_launch_dependents();   // a prep grid of the next piece may take the other SMs
+  const int seq_c0 = sp.seq_off[seq];
+  const int seq_n = sp.seq_off[seq + 1] - seq_c0;
+  const int win_lo = min(sp.c_lo, seq_n), win_hi = min(sp.c_hi, seq_n);
+  const int gc0 = seq_c0 + win_lo;   // this call's first chunk of the sequence
+  const int nch = win_hi - win_lo;
   // this CTA's slice: state rows v in [64 vs, 64 vs + 64)
   const size_t sbase = (static_cast<size_t>(seq) * p.h_v + head) * kHeadDim * kHeadDim +
                        static_cast<size_t>(64 * vs) * kHeadDim;
