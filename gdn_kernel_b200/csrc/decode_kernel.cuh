@@ -159,6 +159,19 @@ __device__ __forceinline__ void unpack16(const uint32_t* w, float* x) {
   }
 }
 
+// 16-byte global -> shared copies that bypass registers (both addresses
+// 16-byte aligned), committed as one group and waited for together.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // Tokens whose inputs a CTA stages in shared memory at a time (T > 1).
 constexpr int kTokGroup = 16;
 
@@ -238,12 +251,15 @@ __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams
 
   const float neg_exp_alog = -expf(p.A_log[h]);
   const float dtb = p.dt_bias[h];
-  // One token step on this thread's rows (inputs already unpacked).
-  auto step = [&](int t, const float* qf, const float* kf, float av, float bv,
+  // Gate and beta of one token (ref kernel.cu:44-53).
+  auto gates = [&](float av, float bv, float& g, float& beta) {
+    g = expf(neg_exp_alog * softplus20(av + dtb));
+    beta = 1.0f / (1.0f + expf(-bv));
+  };
+  // One token step on this thread's rows (inputs already unpacked, gates formed).
+  auto step = [&](int t, const float* qf, const float* kf, float g, float beta,
                   const float* vv) {
     const size_t tok = static_cast<size_t>(bidx) * p.T + t;
-    const float g = expf(neg_exp_alog * softplus20(av + dtb));
-    const float beta = 1.0f / (1.0f + expf(-bv));
     float qk = 0.f;
 #pragma unroll
     for (int e = 0; e < 16; ++e) qk = fmaf(qf[e], kf[e], qk);
@@ -256,10 +272,24 @@ __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams
 #pragma unroll
       for (int e = 0; e < 16; ++e) s[e] = g * st[i][e];
       float dk = 0.f, dq = 0.f;
+      if constexpr (kMulti) {
+        // Several tokens run back to back on the state in registers, so this
+        // product is on the path from one token to the next: four short
+        // chains instead of one of 16.
+        float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        dk = fmaf(s[e], kf[e], dk);
-        dq = fmaf(s[e], qf[e], dq);
+        for (int e = 0; e < 16; ++e) {
+          ak[e & 3] = fmaf(s[e], kf[e], ak[e & 3]);
+          aq[e & 3] = fmaf(s[e], qf[e], aq[e & 3]);
+        }
+        dk = (ak[0] + ak[1]) + (ak[2] + ak[3]);
+        dq = (aq[0] + aq[1]) + (aq[2] + aq[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          dk = fmaf(s[e], kf[e], dk);
+          dq = fmaf(s[e], qf[e], dq);
+        }
       }
 #pragma unroll
       for (int m = 1; m < 8; m <<= 1) {
@@ -290,34 +320,46 @@ __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams
     unpack16(cur.k, kf);
 #pragma unroll
     for (int i = 0; i < kRI; ++i) vv[i] = __bfloat162float(cur.v[i]);
-    step(0, qf, kf, __bfloat162float(cur.a), __bfloat162float(cur.b), vv);
+    float g, beta;
+    gates(__bfloat162float(cur.a), __bfloat162float(cur.b), g, beta);
+    step(0, qf, kf, g, beta, vv);
   } else {
     // Staged token inputs: q and k rows (256 B each), a, b, and this CTA's v rows.
     __shared__ __align__(16) __nv_bfloat16 sq[kTokGroup][kHeadDim];
     __shared__ __align__(16) __nv_bfloat16 sk[kTokGroup][kHeadDim];
     __shared__ float sa[kTokGroup], sb[kTokGroup];
-    __shared__ __nv_bfloat16 sv[kTokGroup][kRows];
+    __shared__ __align__(16) __nv_bfloat16 sv[kTokGroup][kRows];
     const int tid = threadIdx.x;
     for (int t0 = 0; t0 < p.T; t0 += kTokGroup) {
       const int n = min(kTokGroup, p.T - t0);
       __syncthreads();   // the previous group is consumed
-      for (int e = tid; e < n * 16; e += kDecodeThreads) {   // 16 x 16 B per row
+      // The group's q/k rows and this CTA's v entries go straight from global
+      // to shared memory (cp.async, no registers held), all in flight
+      // together: one memory latency per group, which on the first group
+      // overlaps the state rows'.
+      for (int e = tid; e < n * 16; e += kDecodeThreads) {   // 16 x 16 B per q/k row
         const int tt = e >> 4, c = e & 15;
         const size_t qk_off =
             ((static_cast<size_t>(bidx) * p.T + t0 + tt) * p.h_qk + hq) * kHeadDim + 8 * c;
-        reinterpret_cast<uint4*>(&sq[tt][0])[c] = *reinterpret_cast<const uint4*>(p.q + qk_off);
-        reinterpret_cast<uint4*>(&sk[tt][0])[c] = *reinterpret_cast<const uint4*>(p.k + qk_off);
+        cp_async16(&sq[tt][8 * c], p.q + qk_off);
+        cp_async16(&sk[tt][8 * c], p.k + qk_off);
       }
-      for (int e = tid; e < n * kRows; e += kDecodeThreads) {
-        const int tt = e / kRows, r = e % kRows;
-        sv[tt][r] = p.v[((static_cast<size_t>(bidx) * p.T + t0 + tt) * p.h_v + h) * kHeadDim +
-                        rblk * kRows + r];
+      for (int e = tid; e < n * (kRows / 8); e += kDecodeThreads) {   // 16 B of v rows
+        const int tt = e / (kRows / 8), c = e % (kRows / 8);
+        cp_async16(&sv[tt][8 * c],
+                   p.v + ((static_cast<size_t>(bidx) * p.T + t0 + tt) * p.h_v + h) * kHeadDim +
+                       rblk * kRows + 8 * c);
       }
+      cp_async_commit();
+      float ga = 0.f, gb = 0.f;
       if (tid < n) {
         const size_t gate_off = (static_cast<size_t>(bidx) * p.T + t0 + tid) * p.h_v + h;
-        sa[tid] = __bfloat162float(p.a[gate_off]);
-        sb[tid] = __bfloat162float(p.b[gate_off]);
+        ga = __bfloat162float(p.a[gate_off]);
+        gb = __bfloat162float(p.b[gate_off]);
       }
+      cp_async_wait_all();
+      // the group's gates, formed once for all rows (sa = g, sb = beta)
+      if (tid < n) gates(ga, gb, sa[tid], sb[tid]);
       __syncthreads();
       for (int tt = 0; tt < n; ++tt) {
         float qf[16], kf[16], vv[kRI];
