@@ -369,8 +369,9 @@ def time_context_parallel(K, rank, world, flush, total_tokens, iters=3, warmup=1
     return {"tokens": total_tokens, "us": round(ms * 1e3, 1),
             "tokens_per_s": round(total_tokens / (ms * 1e-3), 1),
             "segment_tokens_this_rank": hi - lo,
-            "method": "single call" if world == 1 else
-                      f"context-parallel over {world} ranks (pass A, all-gather, pass B)"}
+            "method": "single call (one sequence in overlapping pieces)" if world == 1 else
+                      f"context-parallel over {world} ranks (rank 0 runs its segment, middle "
+                      f"ranks pass A, all-gather of the affine maps, pass B)"}
 
 
 def prefill_hbm_bytes(lengths, with_state):

@@ -21,9 +21,13 @@ solution/cuda/kernel_prefill.cu:286-293), so each rank
    prepared records, giving its outputs and the state at its segment's end (on
    the last rank: the sequence's final state).
 
-Each rank therefore prepares T/G tokens once and runs three recurrences over
-them (two of them concurrently) instead of the whole chain, and the per-head
-sequential depth drops from T/64 chunks to about 2T/(64 G).  The reference is
+Two ranks need less.  Rank 0 knows its initial state, so it runs its segment
+as one ordinary prefill (the one-sequence pieces path) and reports the map
+(M, N) = (0, S_end): folding it into any state gives its true end state.  The
+last rank's map is folded by no one, so it only prepares, then waits for the
+gather.  Each middle rank prepares T/G tokens once and runs three recurrences
+over them (two of them concurrently) instead of the whole chain, and the
+per-head sequential depth drops from T/64 chunks to about 2T/(64 G).  The reference is
 single-GPU (its harness requests one B200, ref scripts/run_modal.py:36); this
 is the split its recurrence admits.
 
@@ -173,21 +177,48 @@ def cp_prefill(rank: int, world: int, q, k, v, state, A_log, a, dt_bias, b, scal
     T, _, D = q.shape
     h_v = v.shape[1]
     dev = q.device
-    seg = None
-    if T > 0:
+    seg, direct = None, None
+    if T > 0 and rank == 0:
+        # the sequence's own initial state: run the segment outright
+        direct = _run_direct(prefill_fn, q, k, v, state, A_log, a, dt_bias, b, scale)
+        m = torch.zeros(h_v, D, D, dtype=torch.float32, device=dev)
+        n = direct[1]
+    elif T > 0:
         seg = (_FunctionSegment(prefill_fn, q, k, v, A_log, a, dt_bias, b, scale)
                if prefill_fn is not None
                else _KernelSegment(q, k, v, A_log, a, dt_bias, b, scale))
-        m, n = seg.maps()
+        if rank < world - 1:
+            m, n = seg.maps()
+        else:   # no later rank folds the last rank's map
+            m = torch.zeros(h_v, D, D, dtype=torch.float32, device=dev)
+            n = torch.zeros(h_v, D, D, dtype=torch.float32, device=dev)
     else:   # an empty segment maps every state to itself
         m = torch.eye(D, dtype=torch.float32, device=dev).expand(h_v, D, D).contiguous()
         n = torch.zeros(h_v, D, D, dtype=torch.float32, device=dev)
     mine = torch.stack([m, n])
     parts = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(parts, mine, group=group)
+    if direct is not None:
+        return direct
     s_in = fold_states(state, [(p[0], p[1]) for p in parts[:rank]], affine_fn)
     if s_in is None:
         s_in = torch.zeros(h_v, D, D, dtype=torch.float32, device=dev)
     if seg is None:
         return torch.empty(0, h_v, D, dtype=torch.bfloat16, device=dev), s_in.clone()
     return seg.run(s_in)
+
+
+def _run_direct(prefill_fn, q, k, v, state, A_log, a, dt_bias, b, scale):
+    """One segment as an ordinary one-sequence prefill from ``state`` (None =
+    zero): ``(output, end_state)``."""
+    if prefill_fn is None:
+        from .kernel import gdn_prefill
+        prefill_fn = gdn_prefill
+    T, _, D = q.shape
+    h_v = v.shape[1]
+    out = torch.empty(T, h_v, D, dtype=torch.bfloat16, device=q.device)
+    ns = torch.empty(1, h_v, D, D, dtype=torch.float32, device=q.device)
+    cu = torch.tensor([0, T], dtype=torch.int32, device=q.device)
+    st = None if state is None else state.unsqueeze(0).contiguous()
+    prefill_fn(q, k, v, st, A_log, a, dt_bias, b, cu, scale, out, ns)
+    return out, ns[0]
