@@ -71,9 +71,14 @@ int device_setup(unsigned int** status_out) {
     e = cudaFuncSetAttribute(gdn_prefill_prep_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kP1Smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prep smem)");
-    e = cudaFuncSetAttribute(gdn_prefill_chain_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kC2Smem));
+    e = cudaFuncSetAttribute(gdn_prefill_chain_kernel<64>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(ChainLayout<64>::kSmem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem)");
+    e = cudaFuncSetAttribute(gdn_prefill_chain_kernel<128>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(ChainLayout<128>::kSmem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem, wide)");
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
@@ -395,11 +400,23 @@ void launch_prepare(const SplitParams& sp, const CUtensorMap& tq, const CUtensor
               2LL * device_sm_count(), false, st);
 }
 
-// The state recurrence over a prepared workspace (reads it only).
+// The state recurrence over a prepared workspace (reads it only).  A chain
+// CTA owns all 128 of a head's V columns or 64 (two CTAs per head).  The wide
+// CTA does both halves' work in about 1.2x the time per chunk (measured on
+// B200) and loads each record once instead of twice; the narrow one spreads
+// few (sequence, head) pairs n over more SMs.  With one chain CTA per SM, the
+// narrow form takes ceil(2n / SMs) waves of time t and the wide one
+// ceil(n / SMs) waves of 1.2 t, so the wide form wins once 2n > SMs.  (The
+// one-sequence pieces path keeps the narrow form: its idle SMs run the prep.)
 void launch_recur(const SplitParams& sp, const CUtensorMap& tk, const CUtensorMap& tv,
                   int64_t num_seqs, int32_t num_v_heads, cudaStream_t st) {
-  const dim3 g2(static_cast<unsigned>(2 * num_v_heads), static_cast<unsigned>(num_seqs));
-  gdn_prefill_chain_kernel<<<g2, kC2Threads, kC2Smem, st>>>(tk, tv, sp);
+  if (2 * num_seqs * num_v_heads > static_cast<int64_t>(device_sm_count())) {
+    const dim3 g(static_cast<unsigned>(num_v_heads), static_cast<unsigned>(num_seqs));
+    gdn_prefill_chain_kernel<128><<<g, kC2Threads, ChainLayout<128>::kSmem, st>>>(tk, tv, sp);
+  } else {
+    const dim3 g(static_cast<unsigned>(2 * num_v_heads), static_cast<unsigned>(num_seqs));
+    gdn_prefill_chain_kernel<64><<<g, kC2Threads, ChainLayout<64>::kSmem, st>>>(tk, tv, sp);
+  }
 }
 
 // A whole two-stage call.  One short-grid sequence (its chain kernel fills at

@@ -520,8 +520,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
 }
 
 // ---------------------------------------------------------------- chain kernel
-// One CTA per (sequence, v-head, 64-column V slice), warp-specialised:
-//   warps 0-7  state warps: thread (k = row, half) keeps S_s^T[k][32 half + j]
+// One CTA per (sequence, v-head, kVS-column V slice), warp-specialised:
+//   warps 0-7  state warps: thread (k = row, half) keeps S_s^T[k][kVS/2 half + j]
 //              in registers; warps 2,3,6,7 also turn rows 64-127 of D_UO into
 //              the decayed v_new tile; warp 0 issues M2 and M3.  The eight
 //              hand over to one another through two named barriers only;
@@ -534,15 +534,33 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
 //   M3  D_S4      = K^T (v_new e^{gamma_last - gamma})
 //   S_s^T = e^{gamma_last} S_s^T + D_S4   (bf16 copy -> M2 of chunk c + 1)
 // Only M2 -> v_new -> M3 -> state update is serial from chunk to chunk.
-constexpr uint32_t kC2StQW = 0;         // 32 KiB [Q' ; -W]  (record)
-constexpr uint32_t kC2StPT = 32768;     // 16 KiB [P' ; T_b] (record, adjacent there too)
-constexpr uint32_t kC2StK = 49152;      // 16 KiB K chunk [c][kd], two 64-column blocks
-constexpr uint32_t kC2StV = 65536;      // 8 KiB  V chunk, this CTA's 64 columns [c][v]
-constexpr uint32_t kC2StGam = 73728;    // 256 B  gamma (record)
-constexpr uint32_t kC2Stage = 74752;    // 73 KiB per stage (1 KiB multiple)
-constexpr uint32_t kC2OffSB = 2 * kC2Stage;        // 16 KiB S_s^T bf16 [kd][64 v]
-constexpr uint32_t kC2OffVND = kC2OffSB + 16384;   // 8 KiB decayed v_new [c][64 v]
-constexpr uint32_t kC2OffBar = kC2OffVND + 8192;
+// Shared-memory and TMEM layout of a chain CTA that owns kVS of a head's 128
+// V columns (kVS = 64: two CTAs per head; 128: one).  The V, S^T and v_new
+// tiles are kVS / 64 blocks of 64 columns, each block 128B-swizzled.
+template <int kVS>
+struct ChainLayout {
+  static constexpr int kVBlocks = kVS / 64;
+  static constexpr int kCols = kVS / 2;               // state columns per state thread
+  static constexpr uint32_t kStQW = 0;                // 32 KiB [Q' ; -W]  (record)
+  static constexpr uint32_t kStPT = 32768;            // 16 KiB [P' ; T_b] (record, adjacent there too)
+  static constexpr uint32_t kStK = 49152;             // 16 KiB K chunk [c][kd], two 64-column blocks
+  static constexpr uint32_t kStV = 65536;             // V chunk, this CTA's columns [c][v]
+  static constexpr uint32_t kStGam = kStV + 8192 * kVBlocks;   // 256 B gamma (record)
+  static constexpr uint32_t kStage = (kStGam + 256 + 1023) / 1024 * 1024;
+  static constexpr uint32_t kOffSB = 2 * kStage;                  // S_s^T bf16 [kd][v]
+  static constexpr uint32_t kOffVND = kOffSB + 16384 * kVBlocks;  // decayed v_new [c][v]
+  static constexpr uint32_t kOffBar = kOffVND + 8192 * kVBlocks;
+  static constexpr uint32_t kOffTmemPtr = kOffBar + 8 * 19;
+  static constexpr uint32_t kOffAbort = kOffTmemPtr + 16;
+  static constexpr uint32_t kSmem = kOffAbort + 16 + 1024;
+  static constexpr uint32_t kTmUO = 0;                // 2 x kVS columns
+  static constexpr uint32_t kTmS4 = 2 * kVS;          // kVS columns
+  static constexpr uint32_t kTmCols = kVS == 64 ? 256 : 512;
+  static constexpr uint32_t kLoadA = 32768 + 16384 + 8192 * kVBlocks + 256;
+  static_assert(kVS == 64 || kVS == 128, "a chain CTA owns 64 or 128 V columns");
+  static_assert(kSmem <= 232448, "chain CTA shared memory");
+};
+constexpr uint32_t kC2LoadB = 16384;
 // mbarriers (pairs are per stage / D_UO buffer):
 //   LdA, LdB   stage loads landed (record + V; K)
 //   M1         M1 done (loader's commit)          UO    M2 done (warp 0's commit)
@@ -554,14 +572,7 @@ enum : int {
   kC2BarFreeA = 10, kC2BarFreeB = 12, kC2BarKReady = 14, kC2BarS = 16, kC2BarEnd = 17,
   kC2BarEnd2 = 18, kC2NumBars = 19
 };
-constexpr uint32_t kC2OffTmemPtr = kC2OffBar + 8 * kC2NumBars;
-constexpr uint32_t kC2OffAbort = kC2OffTmemPtr + 16;
-constexpr uint32_t kC2Smem = kC2OffAbort + 16 + 1024;
-constexpr uint32_t kC2TmUO = 0;         // 2 x 64 columns
-constexpr uint32_t kC2TmS4 = 128;       // 64 columns
-constexpr uint32_t kC2TmCols = 256;
-constexpr uint32_t kC2LoadA = 32768 + 16384 + 8192 + 256;
-constexpr uint32_t kC2LoadB = 16384;
+static_assert(kC2NumBars == 19, "ChainLayout reserves 19 mbarriers");
 constexpr int kC2StateWarps = 8;
 constexpr int kC2OutWarps = 2;
 constexpr int kC2LoaderWarp = kC2StateWarps + kC2OutWarps;
@@ -573,14 +584,18 @@ __device__ __forceinline__ void state_sync(int id) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(32 * kC2StateWarps) : "memory");
 }
 
+template <int kVS>
 __global__ void __launch_bounds__(kC2Threads, 1)
     gdn_prefill_chain_kernel(const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const SplitParams sp) {
+  using L = ChainLayout<kVS>;
+  constexpr int kCols = L::kCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const PrefillParams& p = sp.base;
-  const int head = blockIdx.x >> 1, vs = blockIdx.x & 1, seq = blockIdx.y;
+  const int head = blockIdx.x / (kHeadDim / kVS), vs = blockIdx.x % (kHeadDim / kVS);
+  const int seq = blockIdx.y;
   const int hq = head / (p.h_v / p.h_qk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_launch_dependents();   // a prep grid of the next piece may take the other SMs
@@ -589,14 +604,14 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   const int win_lo = min(sp.c_lo, seq_n), win_hi = min(sp.c_hi, seq_n);
   const int gc0 = seq_c0 + win_lo;   // this call's first chunk of the sequence
   const int nch = win_hi - win_lo;
-  // this CTA's slice: state rows v in [64 vs, 64 vs + 64)
+  // this CTA's slice: state rows v in [kVS vs, kVS vs + kVS)
   const size_t sbase = (static_cast<size_t>(seq) * p.h_v + head) * kHeadDim * kHeadDim +
-                       static_cast<size_t>(64 * vs) * kHeadDim;
+                       static_cast<size_t>(kVS * vs) * kHeadDim;
 
   if (nch <= 0) {   // ref kernel_prefill.cu:61-66: the state passes through unchanged
     float4* dst = reinterpret_cast<float4*>(p.new_state + sbase);
     const float4* src = p.state ? reinterpret_cast<const float4*>(p.state + sbase) : nullptr;
-    for (int i = tid; i < 64 * kHeadDim / 4; i += kC2Threads)
+    for (int i = tid; i < kVS * kHeadDim / 4; i += kC2Threads)
       dst[i] = src ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     return;
   }
@@ -606,35 +621,39 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   const int clen_last = sp.table[gc0 + nch - 1].clen;
   auto chunk_len = [&](int c) { return c == nch - 1 ? clen_last : kChunk; };
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kC2OffBar);
-  uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + kC2OffTmemPtr);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kC2OffAbort);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + L::kOffTmemPtr);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
 
   auto load_a = [&](int c) {   // record tiles + V of chunk c -> stage c & 1
     const int st = c & 1;
-    uint8_t* stage = smem + st * kC2Stage;
+    uint8_t* stage = smem + st * L::kStage;
     uint64_t* bar = bars + kC2BarLdA + st;
     const uint8_t* rec =
         sp.records + (static_cast<size_t>(gc0 + c) * p.h_v + head) * kRecBytes;
-    mbar_arrive_expect_tx(bar, sp.zero_v ? kC2LoadA - 8192 : kC2LoadA);
-    bulk_load(stage + kC2StQW, rec + kRecOffQW, 32768, bar);
-    bulk_load(stage + kC2StPT, rec + kRecOffP, 16384, bar);
-    bulk_load(stage + kC2StGam, rec + kRecOffGam, 256, bar);
-    if (!sp.zero_v)
-      tma_load_3d(stage + kC2StV, &tm_v, bar, 64 * vs, head, static_cast<int>(cstart0 + 64 * c));
+    mbar_arrive_expect_tx(bar, sp.zero_v ? L::kLoadA - 8192 * L::kVBlocks : L::kLoadA);
+    bulk_load(stage + L::kStQW, rec + kRecOffQW, 32768, bar);
+    bulk_load(stage + L::kStPT, rec + kRecOffP, 16384, bar);
+    bulk_load(stage + L::kStGam, rec + kRecOffGam, 256, bar);
+    if (!sp.zero_v) {
+#pragma unroll
+      for (int b = 0; b < L::kVBlocks; ++b)
+        tma_load_3d(stage + L::kStV + 8192 * b, &tm_v, bar, kVS * vs + 64 * b, head,
+                    static_cast<int>(cstart0 + 64 * c));
+    }
   };
   auto load_b = [&](int c) {   // K of chunk c -> stage c & 1
     const int st = c & 1;
-    uint8_t* stage = smem + st * kC2Stage;
+    uint8_t* stage = smem + st * L::kStage;
     uint64_t* bar = bars + kC2BarLdB + st;
     const int t0 = static_cast<int>(cstart0 + 64 * c);
     mbar_arrive_expect_tx(bar, kC2LoadB);
-    tma_load_3d(stage + kC2StK, &tm_k, bar, 0, hq, t0);
-    tma_load_3d(stage + kC2StK + 8192, &tm_k, bar, 64, hq, t0);
+    tma_load_3d(stage + L::kStK, &tm_k, bar, 0, hq, t0);
+    tma_load_3d(stage + L::kStK + 8192, &tm_k, bar, 64, hq, t0);
   };
 
   if (warp == 0) {
-    tmem_alloc(tmem_ptr, kC2TmCols);
+    tmem_alloc(tmem_ptr, L::kTmCols);
     tmem_relinquish();
   }
   if (warp == kC2LoaderWarp && lane == 0) {
@@ -651,14 +670,24 @@ __global__ void __launch_bounds__(kC2Threads, 1)
       load_b(1);
     }
   }
-  float sreg[32];
+  float sreg[kCols];
   const int quad = warp & 3, half = (warp >> 2) & 1, row = quad * 32 + lane;
+  // This thread's kCols columns of row r of the S^T or v_new tile (64-column
+  // blocks `block_bytes` apart): half of one block (kVS = 64) or block `half`.
+  auto st_cols_bf16 = [&](uint8_t* tile, uint32_t block_bytes, int r, const float* x, float mul) {
+    if constexpr (kVS == 64) {
+      st_half_row_bf16(tile, r, 4 * half, x, mul);
+    } else {
+      st_half_row_bf16(tile + half * block_bytes, r, 0, x, mul);
+      st_half_row_bf16(tile + half * block_bytes, r, 4, x + 32, mul);
+    }
+  };
   if (warp < kC2StateWarps) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < kCols; ++j)
       sreg[j] =
-          p.state ? p.state[sbase + static_cast<size_t>(32 * half + j) * kHeadDim + row] : 0.f;
-    st_half_row_bf16(smem + kC2OffSB, row, 4 * half, sreg, 1.0f);
+          p.state ? p.state[sbase + static_cast<size_t>(kCols * half + j) * kHeadDim + row] : 0.f;
+    st_cols_bf16(smem + L::kOffSB, 16384, row, sreg, 1.0f);
     fence_proxy_async_smem();
   }
   tc_fence_before();
@@ -666,7 +695,7 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_ptr;
   const uint32_t tm_lane = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t idesc_uo = idesc_bf16_f32(128, 64, 0, 1);
+  const uint32_t idesc_uo = idesc_bf16_f32(128, kVS, 0, 1);
 
   // Waits are warp-uniform: every lane polls, and the warp proceeds only if
   // all saw the phase complete (a limit that runs out mid-warp cannot split it).
@@ -730,10 +759,10 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     };
     for (int c = 0; c < nch; ++c) {
       const int st = c & 1;
-      uint8_t* stage = smem + st * kC2Stage;
+      uint8_t* stage = smem + st * L::kStage;
       const int clen = chunk_len(c);
       if (!(ok = warp_wait(kC2BarLdA + st, (c >> 1) & 1, kStatusTmaTimeout))) break;
-      if (clen < kChunk && !sp.zero_v) zero_rows(stage + kC2StV, 1, clen);
+      if (clen < kChunk && !sp.zero_v) zero_rows(stage + L::kStV, L::kVBlocks, clen);
       // M1 into D_UO[st] once the output warps have read its chunk c - 2 (with
       // zero V there is no M1; the commit then only orders the buffer's reuse)
       if (c >= 2 && !(ok = warp_wait(kC2BarOut + st, ((c - 2) >> 1) & 1, kStatusMmaTimeout)))
@@ -744,15 +773,15 @@ __global__ void __launch_bounds__(kC2Threads, 1)
         if (!sp.zero_v) {
 #pragma unroll
           for (int s = 0; s < 4; ++s)
-            umma_bf16(tmem + kC2TmUO + 64 * st, sdesc_sw128(a_st + kC2StPT + s * 32, 16, 1024),
-                      sdesc_sw128(a_st + kC2StV + s * 2048, 8192, 1024), idesc_uo,
+            umma_bf16(tmem + L::kTmUO + kVS * st, sdesc_sw128(a_st + L::kStPT + s * 32, 16, 1024),
+                      sdesc_sw128(a_st + L::kStV + s * 2048, 8192, 1024), idesc_uo,
                       s > 0 ? 1u : 0u);
         }
         umma_commit(bars + kC2BarM1 + st);
       }
       __syncwarp();
       if (!(ok = warp_wait(kC2BarLdB + st, (c >> 1) & 1, kStatusTmaTimeout))) break;
-      if (clen < kChunk) zero_rows(stage + kC2StK, 2, clen);
+      if (clen < kChunk) zero_rows(stage + L::kStK, 2, clen);
       if (elect_one()) mbar_arrive(bars + kC2BarKReady + st);
       __syncwarp();
     }
@@ -762,9 +791,9 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     // Every state warp runs all nch iterations and reaches both named
     // barriers each time, also after a failed wait (the work is then
     // skipped): a warp that left early would strand the others there.
-    const uint32_t a_sb = smem_u32(smem + kC2OffSB);
-    const uint32_t a_vnd = smem_u32(smem + kC2OffVND);
-    const uint32_t idesc_s = idesc_bf16_f32(128, 64, 1, 1);
+    const uint32_t a_sb = smem_u32(smem + L::kOffSB);
+    const uint32_t a_vnd = smem_u32(smem + L::kOffVND);
+    const uint32_t idesc_s = idesc_bf16_f32(128, kVS, 1, 1);
     bool ok = true;
     // Waits on phases that are normally long complete sit in idle slots of
     // the previous step, off the chain: the gammas of chunk c + 1 and (warp 0)
@@ -774,7 +803,7 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     auto gammas = [&](int c) {   // chunk c's gamma_last and this row's v_new decay
       ok = ok && warp_wait(kC2BarLdA + (c & 1), (c >> 1) & 1, kStatusTmaTimeout);
       if (ok) {
-        const float* gam = reinterpret_cast<const float*>(smem + (c & 1) * kC2Stage + kC2StGam);
+        const float* gam = reinterpret_cast<const float*>(smem + (c & 1) * L::kStage + L::kStGam);
         const int clen = chunk_len(c), cc = row - 64;
         gam_last = gam[clen - 1];
         dec = (quad >= 2 && cc < clen) ? __expf(gam_last - gam[cc]) : 0.f;
@@ -784,14 +813,14 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     if (warp == 0) ok = ok && warp_wait(kC2BarM1, 0, kStatusMmaTimeout);
     for (int c = 0; c < nch; ++c) {
       const int st = c & 1;
-      const uint32_t a_st = smem_u32(smem + st * kC2Stage);
+      const uint32_t a_st = smem_u32(smem + st * L::kStage);
       if (warp == 0) {   // M2 (M1 of this chunk is complete), then K of this chunk
         if (ok) {
           tc_fence_after();
 #pragma unroll
           for (int s = 0; s < 8; ++s)
-            umma_bf16_elect(tmem + kC2TmUO + 64 * st,
-                            sdesc_sw128(a_st + kC2StQW + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
+            umma_bf16_elect(tmem + L::kTmUO + kVS * st,
+                            sdesc_sw128(a_st + L::kStQW + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024),
                             sdesc_sw128(a_sb + s * 2048, 16384, 1024), idesc_uo,
                             (s > 0 || !sp.zero_v) ? 1u : 0u);
           umma_commit_elect(bars + kC2BarUO + st);
@@ -802,10 +831,14 @@ __global__ void __launch_bounds__(kC2Threads, 1)
         ok = ok && warp_wait(kC2BarUO + st, (c >> 1) & 1, kStatusMmaTimeout);
         if (ok) {
           tc_fence_after();
-          float r[32];
-          tmem_ld32(tmem + kC2TmUO + 64 * st + tm_lane + 32 * half, r);
+          float r[kCols];
+          if constexpr (kCols == 32) {
+            tmem_ld32(tmem + L::kTmUO + kVS * st + tm_lane + kCols * half, r);
+          } else {
+            tmem_ld64(tmem + L::kTmUO + kVS * st + tm_lane + kCols * half, r);
+          }
           tmem_wait_ld();
-          st_half_row_bf16(smem + kC2OffVND, row - 64, 4 * half, r, dec);
+          st_cols_bf16(smem + L::kOffVND, 8192, row - 64, r, dec);
           fence_proxy_async_smem();
         }
       }
@@ -816,7 +849,7 @@ __global__ void __launch_bounds__(kC2Threads, 1)
         tc_fence_after();
 #pragma unroll
         for (int s = 0; s < 4; ++s)
-          umma_bf16_elect(tmem + kC2TmS4, sdesc_sw128(a_st + kC2StK + s * 2048, 8192, 1024),
+          umma_bf16_elect(tmem + L::kTmS4, sdesc_sw128(a_st + L::kStK + s * 2048, 8192, 1024),
                           sdesc_sw128(a_vnd + s * 2048, 8192, 1024), idesc_s, s > 0 ? 1u : 0u);
         umma_commit_elect(bars + kC2BarS);
         if (elect_one()) mbar_arrive(bars + kC2BarFreeA + st);
@@ -829,12 +862,16 @@ __global__ void __launch_bounds__(kC2Threads, 1)
       ok = ok && warp_wait(kC2BarS, c & 1, kStatusMmaTimeout);
       if (ok) {   // S_s^T = e^{gamma_last} S_s^T + D_S4
         tc_fence_after();
-        float r[32];
-        tmem_ld32(tmem + kC2TmS4 + tm_lane + 32 * half, r);
+        float r[kCols];
+        if constexpr (kCols == 32) {
+          tmem_ld32(tmem + L::kTmS4 + tm_lane + kCols * half, r);
+        } else {
+          tmem_ld64(tmem + L::kTmS4 + tm_lane + kCols * half, r);
+        }
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sreg[j] = fmaf(decay, sreg[j], r[j]);
-        st_half_row_bf16(smem + kC2OffSB, row, 4 * half, sreg, 1.0f);
+        for (int j = 0; j < kCols; ++j) sreg[j] = fmaf(decay, sreg[j], r[j]);
+        st_cols_bf16(smem + L::kOffSB, 16384, row, sreg, 1.0f);
         fence_proxy_async_smem();
         if (warp == 0) {
           if (elect_one()) mbar_arrive(bars + kC2BarFreeB + st);
@@ -852,22 +889,30 @@ __global__ void __launch_bounds__(kC2Threads, 1)
       const int st = c & 1;
       if (!warp_wait(kC2BarUO + st, (c >> 1) & 1, kStatusMmaTimeout)) break;
       tc_fence_after();
-      float r[64];
-      tmem_ld64(tmem + kC2TmUO + 64 * st + tm_lane, r);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bars + kC2BarOut + st);
-      if (p.out && orow < chunk_len(c)) {
-        __nv_bfloat16* o = p.out + (static_cast<size_t>(cstart0 + 64 * c + orow) * p.h_v + head) *
-                                       kHeadDim + 64 * vs;
+      // kVS / 64 blocks of 64 columns; D_UO[st] is released after the last
+      // block's TMEM read, before that block's global stores
+      const bool write = p.out && orow < chunk_len(c);
+      __nv_bfloat16* o = p.out + (static_cast<size_t>(cstart0 + 64 * c + orow) * p.h_v + head) *
+                                     kHeadDim + kVS * vs;
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          uint4 u;
-          u.x = pack_bf16x2(p.scale * r[8 * cc + 0], p.scale * r[8 * cc + 1]);
-          u.y = pack_bf16x2(p.scale * r[8 * cc + 2], p.scale * r[8 * cc + 3]);
-          u.z = pack_bf16x2(p.scale * r[8 * cc + 4], p.scale * r[8 * cc + 5]);
-          u.w = pack_bf16x2(p.scale * r[8 * cc + 6], p.scale * r[8 * cc + 7]);
-          *reinterpret_cast<uint4*>(o + 8 * cc) = u;
+      for (int b = 0; b < L::kVBlocks; ++b) {
+        float r[64];
+        tmem_ld64(tmem + L::kTmUO + kVS * st + tm_lane + 64 * b, r);
+        if (b == L::kVBlocks - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bars + kC2BarOut + st);
+        }
+        if (write) {
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            uint4 u;
+            u.x = pack_bf16x2(p.scale * r[8 * cc + 0], p.scale * r[8 * cc + 1]);
+            u.y = pack_bf16x2(p.scale * r[8 * cc + 2], p.scale * r[8 * cc + 3]);
+            u.z = pack_bf16x2(p.scale * r[8 * cc + 4], p.scale * r[8 * cc + 5]);
+            u.w = pack_bf16x2(p.scale * r[8 * cc + 6], p.scale * r[8 * cc + 7]);
+            *reinterpret_cast<uint4*>(o + 64 * b + 8 * cc) = u;
+          }
         }
       }
     }
@@ -877,10 +922,10 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   tc_fence_after();
   if (!*abort_flag && warp < kC2StateWarps) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      p.new_state[sbase + static_cast<size_t>(32 * half + j) * kHeadDim + row] = sreg[j];
+    for (int j = 0; j < kCols; ++j)
+      p.new_state[sbase + static_cast<size_t>(kCols * half + j) * kHeadDim + row] = sreg[j];
   }
-  if (warp == 0) tmem_dealloc(tmem, kC2TmCols);
+  if (warp == 0) tmem_dealloc(tmem, L::kTmCols);
 }
 
 }  // namespace gdn

@@ -196,3 +196,27 @@ def test_one_sequence_pieces_bitwise(T, with_state, in_place):
     if T <= 1500:
         ro, rs = _oracle(x)
         assert_prefill_close(o1.cpu(), s1.cpu(), ro, rs)
+
+
+def test_wide_chain_matches_per_sequence_calls():
+    """Three or more sequences run one 128-column chain CTA per (sequence, head);
+    a single sequence runs 64-column CTAs (and, long enough, in pieces).  The
+    same chunks give the same bits either way."""
+    lengths = [700, 4000, 1, 2500]
+    x = W.make_prefill_inputs(lengths, seed=31)
+    d = {n: to_dev(getattr(x, n)) for n in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b")}
+    out, ns = K.prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
+                        d["b"], to_dev(x.cu_seqlens), x.scale)
+    lo = 0
+    for i, n in enumerate(lengths):
+        cu = torch.tensor([0, n], dtype=torch.int32, device="cuda")
+        o1, s1 = K.prefill(d["q"][lo:lo + n], d["k"][lo:lo + n], d["v"][lo:lo + n],
+                           d["state"][i:i + 1].contiguous(), d["A_log"], d["a"][lo:lo + n],
+                           d["dt_bias"], d["b"][lo:lo + n], cu, x.scale)
+        assert torch.equal(o1, out[lo:lo + n]), i
+        assert torch.equal(s1[0], ns[i]), i
+        lo += n
+    torch.cuda.synchronize()
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+    ro, rs = _oracle(x)
+    assert_prefill_close(out.cpu(), ns.cpu(), ro, rs)
