@@ -388,7 +388,13 @@ void launch_prep(const SplitParams& sp, const CUtensorMap& tq, const CUtensorMap
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, gdn_prefill_prep_kernel, tq, tk, sp);
+  if (cudaLaunchKernelEx(&cfg, gdn_prefill_prep_kernel, tq, tk, sp) != cudaSuccess) {
+    // Without the overlap the grid simply runs after the chain before it (same
+    // results); a launch that fails again leaves its error for the caller.
+    (void)cudaGetLastError();
+    gdn_prefill_prep_kernel<<<static_cast<unsigned>(ctas), kPrefillThreads, kP1Smem, st>>>(tq, tk,
+                                                                                          sp);
+  }
 }
 
 // Chunk table and per-(chunk, v-head) records into the workspace.
