@@ -180,8 +180,12 @@ constexpr int kTokGroup = 16;
 // straight to registers.  kMulti = true stages the inputs of up to kTokGroup tokens in
 // shared memory with one round of loads, so the per-token steps do not each
 // wait out a global-memory latency.
+// The bf16-pool one-token instance is held to 6 CTAs per SM (80 registers, a
+// few spilled): with its state packed that keeps more state bytes in flight
+// per SM than 4 spill-free CTAs do (27.7 against 30.6 us at B=64 on B200).
 template <typename StateT, bool kMulti, bool kHasState>
-__global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 2) ? 6 : 0)
+    gdn_decode_kernel(DecodeParams p) {
   using L = DecodeLayout<StateT>;
   constexpr int kVec = L::kVec, kAcc = L::kAcc, kRI = L::kRowIters;
   constexpr int kRows = 16 * kRI;   // rows per CTA: 4 warps x 4 rows x kRowIters
@@ -229,6 +233,83 @@ __global__ void __launch_bounds__(kDecodeThreads) gdn_decode_kernel(DecodeParams
         for (int i = 0; i < kRI; ++i)
           p.out[((static_cast<size_t>(bidx) * p.T + t) * p.h_v + h) * kHeadDim + row0 + 4 * i] =
               __float2bfloat16(0.f);
+    return;
+  }
+
+  if constexpr (sizeof(StateT) == 2 && !kMulti && kHasState) {
+    // bf16 pool, one token.  The state rows stay packed, two bf16 per 32-bit
+    // register (32 registers instead of 64 floats), and are unpacked row by
+    // row: fewer registers per thread, more CTAs and so more state bytes in
+    // flight per SM.  The arithmetic and its order are those of the general
+    // path below, so the results are the same bits.
+    const size_t base = (ridx * p.h_v + h) * hd2 + static_cast<size_t>(row0) * kHeadDim + kVec * l8;
+    const __nv_bfloat16* srcb = static_cast<const __nv_bfloat16*>(p.pool) + base;
+    uint32_t raw[kRI][8];
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        asm volatile("ld.global.L1::no_allocate.L2::256B.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(raw[i][4 * j]), "=r"(raw[i][4 * j + 1]), "=r"(raw[i][4 * j + 2]),
+                       "=r"(raw[i][4 * j + 3])
+                     : "l"(srcb + 4 * i * kHeadDim + 8 * kVec * j));
+    auto unpack2 = [](uint32_t w) {
+      return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+    };
+    const float g = expf(-expf(p.A_log[h]) * softplus20(__bfloat162float(cur.a) + p.dt_bias[h]));
+    const float beta = 1.0f / (1.0f + expf(-__bfloat162float(cur.b)));
+    float qk = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float2 q2 = unpack2(cur.q[w]), k2 = unpack2(cur.k[w]);
+      qk = fmaf(q2.x, k2.x, qk);
+      qk = fmaf(q2.y, k2.y, qk);
+    }
+    qk += __shfl_xor_sync(0xffffffffu, qk, 1);
+    qk += __shfl_xor_sync(0xffffffffu, qk, 2);
+    qk += __shfl_xor_sync(0xffffffffu, qk, 4);
+#pragma unroll
+    for (int i = 0; i < kRI; ++i) {
+      float dk = 0.f, dq = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float2 s2 = unpack2(raw[i][w]), k2 = unpack2(cur.k[w]), q2 = unpack2(cur.q[w]);
+        const float sx = g * s2.x, sy = g * s2.y;
+        dk = fmaf(sx, k2.x, dk);
+        dq = fmaf(sx, q2.x, dq);
+        dk = fmaf(sy, k2.y, dk);
+        dq = fmaf(sy, q2.y, dq);
+      }
+#pragma unroll
+      for (int m = 1; m < 8; m <<= 1) {
+        dk += __shfl_xor_sync(0xffffffffu, dk, m);
+        dq += __shfl_xor_sync(0xffffffffu, dq, m);
+      }
+      const float delta = beta * (__bfloat162float(cur.v[i]) - dk);
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float2 s2 = unpack2(raw[i][w]), k2 = unpack2(cur.k[w]);
+        raw[i][w] = pack_bf16x2(fmaf(delta, k2.x, g * s2.x), fmaf(delta, k2.y, g * s2.y));
+      }
+      if (l8 == 0)
+        p.out[(static_cast<size_t>(bidx) * p.h_v + h) * kHeadDim + row0 + 4 * i] =
+            __float2bfloat16(p.scale * (dq + delta * qk));
+    }
+    auto store_rows = [&](__nv_bfloat16* dst) {
+#pragma unroll
+      for (int i = 0; i < kRI; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(
+                           dst + 4 * i * kHeadDim + 8 * kVec * j),
+                       "r"(raw[i][4 * j]), "r"(raw[i][4 * j + 1]), "r"(raw[i][4 * j + 2]),
+                       "r"(raw[i][4 * j + 3])
+                       : "memory");
+    };
+    if (p.inter)   // the state after the token, at [read slot, 0]
+      store_rows(static_cast<__nv_bfloat16*>(p.inter) + base);
+    store_rows(static_cast<__nv_bfloat16*>(p.new_pool) + (widx * p.h_v + h) * hd2 +
+               static_cast<size_t>(row0) * kHeadDim + kVec * l8);
     return;
   }
 
