@@ -26,10 +26,12 @@ def test_state_affine_kernel_matches_fp32_matmul():
     torch.testing.assert_close(n2.double(), ref, atol=1e-4, rtol=1e-5)
 
 
-def test_prepare_then_recur_equals_prefill():
+@pytest.mark.parametrize("lengths", [[300, 0, 64, 1, 129], [300, 129]])
+def test_prepare_then_recur_equals_prefill(lengths):
     """The two stages as separate calls give the single call's results bitwise;
-    a null V equals an all-zero V; a null output changes nothing else."""
-    lengths = [300, 0, 64, 1, 129]
+    a null V equals an all-zero V; a null output changes nothing else.  Five
+    sequences run 128-column chain CTAs (2 x 5 x 32 > SMs), two run 64-column
+    ones."""
     x = W.make_prefill_inputs(lengths, seed=17, device="cuda")
     T, N = sum(lengths), len(lengths)
     ws = torch.empty(K.prefill_workspace_bytes(N, T, 32), dtype=torch.uint8, device="cuda")
