@@ -239,10 +239,11 @@ __device__ __forceinline__ void st_tp_pair(uint8_t* tpzt, int i, int j, float t0
 }
 
 // T = (I - A)^{-1} for the strictly lower 64x64 fp32 A (row pitch kLdA), by
-// block doubling from 16x16 diagonal blocks:
-//   1. the four 16x16 diagonal blocks T_bb = (I - A_bb)^{-1}: lanes 0-15 /
-//      16-31 of warps 0 and 1 each solve one column of one block by forward
-//      substitution with the column in registers;
+// block doubling from 8x8 diagonal blocks:
+//   1. the four 16x16 diagonal blocks T_bb = (I - A_bb)^{-1}: eight lanes of
+//      warps 0 and 1 per 8x8 sub-block each solve one column by forward
+//      substitution (8 dependent steps), then warps 0-3 form each block's
+//      lower 8x8 part T_10 = T_11 (A_10 T_00) in fp32;
 //   2. 16 -> 32: in each 32x32 diagonal block, T_10 = T_11 (A_10 T_00) as two
 //      16x16 products (warps 0-3, one 16x8 tile each);
 //   3. 32 -> 64: T_10 = T_11 (A_10 T_00) as two 32x32 products (all 8 warps).
@@ -257,14 +258,13 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
                                                  const float* bet, const float* eg, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   constexpr int kLdC = 40;    // pitch of the 32x32 scratch tile (conflict-free B fragments)
-  if (warp < 2) {   // step 1: block 2 warp + lane / 16, column lane % 16
-    const int o = 16 * (2 * warp + (lane >> 4)), j = lane & 15;
-    float x[16];
+  if (warp < 2) {   // step 1a: 8x8 sub-block 4 warp + lane / 8, column lane % 8
+    const int o = 8 * (4 * warp + (lane >> 3)), j = lane & 7;
+    float x[8];
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      // four partial sums (one per float4 lane) keep the dependent FMA chain
-      // of each row short; only the newest x enters through the last FMA
-      float acc[4] = {(m == j) ? 1.0f : 0.0f, 0.f, 0.f, 0.f};
+    for (int m = 0; m < 8; ++m) {
+      // two partial sums keep the dependent chain short; the newest x enters last
+      float acc[2] = {(m == j) ? 1.0f : 0.0f, 0.f};
       const float4* rp = reinterpret_cast<const float4*>(A + (o + m) * kLdA + o);
 #pragma unroll
       for (int q = 0; q < (m + 3) / 4; ++q) {
@@ -272,15 +272,23 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
         const float av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          if (4 * q + e < m) acc[e] = fmaf(av[e], x[4 * q + e], acc[e]);
+          if (4 * q + e < m) acc[e & 1] = fmaf(av[e], x[4 * q + e], acc[e & 1]);
       }
-      x[m] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      x[m] = acc[0] + acc[1];
     }
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
+    for (int m = 0; m < 8; ++m) {
       T[(o + m) * kLdA + o + j] = x[m];
       st_tp_one(tpzt, o + m, o + j, x[m], bet, eg);
     }
+  } else if (warp < 4) {   // zeros of the upper-right 8x8 blocks inside the 16x16 diagonal blocks
+    const int t = tid - 64;                                  // 64 threads
+    const int blk = t >> 4, r = (t >> 1) & 7, part = t & 1;  // block, row, half row
+    const int rr = 16 * blk + r, c0 = 16 * blk + 8 + 4 * part;
+    *reinterpret_cast<float4*>(T + rr * kLdA + c0) = make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t off = sw128_off(rr, (16 * blk + 8) / 8);
+    *reinterpret_cast<uint2*>(tpzt + off + 8 * part) = make_uint2(0, 0);
+    *reinterpret_cast<uint2*>(tpzt + 24576 + off + 8 * part) = make_uint2(0, 0);
   } else if (warp >= 4) {   // zeros of the upper-right 16x16 blocks inside the 32x32 diagonal blocks
     const int t = tid - 128;             // 128 threads
     const int blk = t >> 6, r = (t >> 2) & 15, part = t & 3;   // block, row, quarter row
@@ -291,6 +299,32 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
       *reinterpret_cast<uint4*>(tpzt + off) = make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(tpzt + 24576 + off) = make_uint4(0, 0, 0, 0);
     }
+  }
+  if (warp < 4) {   // step 1b: 8 -> 16 in diagonal block b = warp: T_10 = T_11 (A_10 T_00), fp32
+    named_sync(3, 128);   // warps 0-3: the 8x8 diagonal blocks and the zeros are written
+    const int o = 16 * warp;
+    const int r = lane >> 2, c = 2 * (lane & 3);             // rows r, columns c, c + 1
+    float* Xb = X + warp * 64;                               // 8x8 scratch, pitch 8
+    float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float a = A[(o + 8 + r) * kLdA + o + k];
+      y0 = fmaf(a, T[(o + k) * kLdA + o + c], y0);
+      y1 = fmaf(a, T[(o + k) * kLdA + o + c + 1], y1);
+    }
+    Xb[r * 8 + c] = y0;
+    Xb[r * 8 + c + 1] = y1;
+    __syncwarp();
+    float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float tk = T[(o + 8 + r) * kLdA + o + 8 + k];
+      t0 = fmaf(tk, Xb[k * 8 + c], t0);
+      t1 = fmaf(tk, Xb[k * 8 + c + 1], t1);
+    }
+    T[(o + 8 + r) * kLdA + o + c] = t0;
+    T[(o + 8 + r) * kLdA + o + c + 1] = t1;
+    st_tp_pair(tpzt, o + 8 + r, o + c, t0, t1, bet, eg);
   }
   __syncthreads();
   const int g = lane >> 2, t = lane & 3;
