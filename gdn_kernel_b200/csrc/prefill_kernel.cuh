@@ -335,8 +335,9 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
     float* Xp = X + 16 * B + 8 * nt;
     *reinterpret_cast<float2*>(Xp + g * kLdC + 2 * t) = make_float2(d[0], d[1]);
     *reinterpret_cast<float2*>(Xp + (g + 8) * kLdC + 2 * t) = make_float2(d[2], d[3]);
+    // step 2b reads exactly the X_B tile this warp wrote
+    __syncwarp();
   }
-  __syncthreads();
   if (warp < 4) {   // step 2b: T[32B+16.., 32B..] = T_11 X_B
     const int B = warp >> 1, nt = warp & 1, o = 32 * B;
     float d[4];
@@ -356,7 +357,8 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
     *reinterpret_cast<float2*>(Xp + g * kLdC + 2 * t) = make_float2(d[0], d[1]);
     *reinterpret_cast<float2*>(Xp + (g + 8) * kLdC + 2 * t) = make_float2(d[2], d[3]);
   }
-  __syncthreads();
+  // step 3b of column block nt reads the two 16-row halves warps nt and nt + 4 wrote
+  named_sync(4 + nt, 64);
   {  // step 3b: T[32:64, 0:32] = T[32:64, 32:64] X  (only the bf16 tiles need it)
     float d[4];
     mma_tile_tf32<4>(d, T + (32 + 16 * mt) * kLdA + 32, kLdA, X + 8 * nt, kLdC, lane);
