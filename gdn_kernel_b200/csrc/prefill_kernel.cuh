@@ -325,8 +325,10 @@ __device__ __forceinline__ void solve_unit_lower(const float* A, float* T, float
     T[(o + 8 + r) * kLdA + o + c] = t0;
     T[(o + 8 + r) * kLdA + o + c + 1] = t1;
     st_tp_pair(tpzt, o + 8 + r, o + c, t0, t1, bet, eg);
+    // step 2a reads the 16x16 diagonal blocks warps 0-3 just completed; the
+    // zeros of warps 4-7 are first read by step 3a, after the next CTA barrier
+    named_sync(3, 128);
   }
-  __syncthreads();
   const int g = lane >> 2, t = lane & 3;
   if (warp < 4) {   // step 2a: X_B = A[32B+16.., 32B..] T[32B.., 32B..] (16x16, tile nt of block B)
     const int B = warp >> 1, nt = warp & 1, o = 32 * B;
