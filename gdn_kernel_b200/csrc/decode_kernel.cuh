@@ -171,6 +171,26 @@ __device__ __forceinline__ void cp_async_commit() {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
+// All but the most recently committed group have landed.
+__device__ __forceinline__ void cp_async_wait_group1() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// kVec state elements from shared memory as floats (the layout of ld_vec).
+__device__ __forceinline__ void ld_vec_smem(const float* p, float* x) {
+  const float4 r = *reinterpret_cast<const float4*>(p);
+  x[0] = r.x; x[1] = r.y; x[2] = r.z; x[3] = r.w;
+}
+__device__ __forceinline__ void ld_vec_smem(const __nv_bfloat16* p, float* x) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
 
 // Tokens whose inputs a CTA stages in shared memory at a time (T > 1).
 constexpr int kTokGroup = 16;
@@ -190,15 +210,20 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
   constexpr int kVec = L::kVec, kAcc = L::kAcc, kRI = L::kRowIters;
   constexpr int kRows = 16 * kRI;   // rows per CTA: 4 warps x 4 rows x kRowIters
   constexpr int kCtasPerHead = kHeadDim / kRows;
-  const int bh = blockIdx.x / kCtasPerHead;   // batch * H_v + v-head
-  const int rblk = blockIdx.x % kCtasPerHead;
+  // Multi-token calls of up to kTokGroup tokens give each CTA two consecutive
+  // row blocks: the second block's state streams into shared memory while the
+  // first block's tokens run (decode_pair_blocks).
+  const bool pair = kMulti && p.T <= kTokGroup;
+  const int per_head = pair ? kCtasPerHead / 2 : kCtasPerHead;
+  const int bh = blockIdx.x / per_head;   // batch * H_v + v-head
+  const int rblk = (blockIdx.x % per_head) * (pair ? 2 : 1);
   const int h = bh % p.h_v;
   const int bidx = bh / p.h_v;
   const int hq = h / (p.h_v / p.h_qk);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int l8 = lane & 7;
-  const int row0 = rblk * kRows + warp * (4 * kRI) + (lane >> 3);   // rows row0 + 4 i
+  int row0 = rblk * kRows + warp * (4 * kRI) + (lane >> 3);   // rows row0 + 4 i (this block)
   const size_t hd2 = static_cast<size_t>(kHeadDim) * kHeadDim;
 
   // Token inputs of token t (issued before they are needed: the slot index
@@ -229,10 +254,11 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
   if (ridx < 0 || widx < 0) {   // padding entry: zero outputs, no state traffic
     if (l8 == 0)
       for (int t = 0; t < p.T; ++t)
+        for (int blk = 0; blk < (pair ? 2 : 1); ++blk)
 #pragma unroll
-        for (int i = 0; i < kRI; ++i)
-          p.out[((static_cast<size_t>(bidx) * p.T + t) * p.h_v + h) * kHeadDim + row0 + 4 * i] =
-              __float2bfloat16(0.f);
+          for (int i = 0; i < kRI; ++i)
+            p.out[((static_cast<size_t>(bidx) * p.T + t) * p.h_v + h) * kHeadDim + row0 +
+                  blk * kRows + 4 * i] = __float2bfloat16(0.f);
     return;
   }
 
@@ -409,8 +435,41 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
     __shared__ __align__(16) __nv_bfloat16 sq[kTokGroup][kHeadDim];
     __shared__ __align__(16) __nv_bfloat16 sk[kTokGroup][kHeadDim];
     __shared__ float sa[kTokGroup], sb[kTokGroup];
-    __shared__ __align__(16) __nv_bfloat16 sv[kTokGroup][kRows];
+    __shared__ __align__(16) __nv_bfloat16 sv[kTokGroup][2 * kRows];
+    __shared__ __align__(16) StateT sst[kRows][kHeadDim];   // the second row block's state
     const int tid = threadIdx.x;
+    const int vrows = pair ? 2 * kRows : kRows;
+    // One staged token group's steps on this thread's rows.
+    auto run_tokens = [&](int t0, int n) {
+        for (int tt = 0; tt < n; ++tt) {
+          float qf[16], kf[16], vv[kRI];
+#pragma unroll
+          for (int j = 0; j < kAcc; ++j) {
+            uint32_t wq[kVec / 2], wk[kVec / 2];
+            if constexpr (kVec == 4) {
+              const uint2 uq = *reinterpret_cast<const uint2*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
+              const uint2 uk = *reinterpret_cast<const uint2*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
+              wq[0] = uq.x; wq[1] = uq.y; wk[0] = uk.x; wk[1] = uk.y;
+            } else {
+              const uint4 uq = *reinterpret_cast<const uint4*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
+              const uint4 uk = *reinterpret_cast<const uint4*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
+              wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
+              wk[0] = uk.x; wk[1] = uk.y; wk[2] = uk.z; wk[3] = uk.w;
+            }
+#pragma unroll
+            for (int w = 0; w < kVec / 2; ++w) {
+              const float2 fq = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wq[w]));
+              const float2 fk = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wk[w]));
+              qf[kVec * j + 2 * w] = fq.x; qf[kVec * j + 2 * w + 1] = fq.y;
+              kf[kVec * j + 2 * w] = fk.x; kf[kVec * j + 2 * w + 1] = fk.y;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < kRI; ++i)
+            vv[i] = __bfloat162float(sv[tt][row0 - rblk * kRows + 4 * i]);
+          step(t0 + tt, qf, kf, sa[tt], sb[tt], vv);
+        }
+    };
     for (int t0 = 0; t0 < p.T; t0 += kTokGroup) {
       const int n = min(kTokGroup, p.T - t0);
       __syncthreads();   // the previous group is consumed
@@ -425,51 +484,58 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
         cp_async16(&sq[tt][8 * c], p.q + qk_off);
         cp_async16(&sk[tt][8 * c], p.k + qk_off);
       }
-      for (int e = tid; e < n * (kRows / 8); e += kDecodeThreads) {   // 16 B of v rows
-        const int tt = e / (kRows / 8), c = e % (kRows / 8);
+      for (int e = tid; e < n * (vrows / 8); e += kDecodeThreads) {   // 16 B of v rows
+        const int tt = e / (vrows / 8), c = e % (vrows / 8);
         cp_async16(&sv[tt][8 * c],
                    p.v + ((static_cast<size_t>(bidx) * p.T + t0 + tt) * p.h_v + h) * kHeadDim +
                        rblk * kRows + 8 * c);
       }
       cp_async_commit();
+      if (pair) {   // the second block's state rows, a later group: still in flight below
+        constexpr int kChunksPerRow = kHeadDim * static_cast<int>(sizeof(StateT)) / 16;
+        const StateT* src2 = static_cast<const StateT*>(p.pool) + (ridx * p.h_v + h) * hd2 +
+                             static_cast<size_t>(rblk + 1) * kRows * kHeadDim;
+        for (int e = tid; e < kRows * kChunksPerRow; e += kDecodeThreads) {
+          const int r = e / kChunksPerRow, c = e % kChunksPerRow;
+          cp_async16(reinterpret_cast<uint8_t*>(&sst[r][0]) + 16 * c,
+                     reinterpret_cast<const uint8_t*>(src2 + static_cast<size_t>(r) * kHeadDim) +
+                         16 * c);
+        }
+        cp_async_commit();
+      }
       float ga = 0.f, gb = 0.f;
       if (tid < n) {
         const size_t gate_off = (static_cast<size_t>(bidx) * p.T + t0 + tid) * p.h_v + h;
         ga = __bfloat162float(p.a[gate_off]);
         gb = __bfloat162float(p.b[gate_off]);
       }
-      cp_async_wait_all();
+      if (pair) cp_async_wait_group1();   // the token group has landed
+      else cp_async_wait_all();
       // the group's gates, formed once for all rows (sa = g, sb = beta)
       if (tid < n) gates(ga, gb, sa[tid], sb[tid]);
       __syncthreads();
-      for (int tt = 0; tt < n; ++tt) {
-        float qf[16], kf[16], vv[kRI];
+      run_tokens(t0, n);
+    }
+    if (pair) {
+      // First block done: its state out, then the second block's from shared
+      // memory, and the same staged tokens (one group: T <= kTokGroup) again.
+      StateT* dst1 = static_cast<StateT*>(p.new_pool) + (widx * p.h_v + h) * hd2 +
+                     static_cast<size_t>(row0) * kHeadDim + kVec * l8;
 #pragma unroll
-        for (int j = 0; j < kAcc; ++j) {
-          uint32_t wq[kVec / 2], wk[kVec / 2];
-          if constexpr (kVec == 4) {
-            const uint2 uq = *reinterpret_cast<const uint2*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
-            const uint2 uk = *reinterpret_cast<const uint2*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
-            wq[0] = uq.x; wq[1] = uq.y; wk[0] = uk.x; wk[1] = uk.y;
-          } else {
-            const uint4 uq = *reinterpret_cast<const uint4*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
-            const uint4 uk = *reinterpret_cast<const uint4*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
-            wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
-            wk[0] = uk.x; wk[1] = uk.y; wk[2] = uk.z; wk[3] = uk.w;
-          }
+      for (int i = 0; i < kRI; ++i)
 #pragma unroll
-          for (int w = 0; w < kVec / 2; ++w) {
-            const float2 fq = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wq[w]));
-            const float2 fk = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wk[w]));
-            qf[kVec * j + 2 * w] = fq.x; qf[kVec * j + 2 * w + 1] = fq.y;
-            kf[kVec * j + 2 * w] = fk.x; kf[kVec * j + 2 * w + 1] = fk.y;
-          }
-        }
+        for (int j = 0; j < kAcc; ++j)
+          st_vec(dst1 + 4 * i * kHeadDim + 8 * kVec * j, st[i] + kVec * j);
+      cp_async_wait_all();
+      __syncthreads();
+      row0 += kRows;
 #pragma unroll
-        for (int i = 0; i < kRI; ++i)
-          vv[i] = __bfloat162float(sv[tt][row0 - rblk * kRows + 4 * i]);
-        step(t0 + tt, qf, kf, sa[tt], sb[tt], vv);
-      }
+      for (int i = 0; i < kRI; ++i)
+#pragma unroll
+        for (int j = 0; j < kAcc; ++j)
+          ld_vec_smem(&sst[row0 - (rblk + 1) * kRows + 4 * i][kVec * l8 + 8 * kVec * j],
+                      st[i] + kVec * j);
+      run_tokens(0, p.T);
     }
   }
   StateT* dst = static_cast<StateT*>(p.new_pool) + (widx * p.h_v + h) * hd2 +
@@ -490,14 +556,17 @@ constexpr int decode_ctas_per_head() {
 // whether there is a state (multi-token and pooled calls always have one).
 inline void launch_decode(const DecodeParams& p, long long batch, bool state_bf16,
                           cudaStream_t st) {
+  // multi-token calls of up to kTokGroup tokens: two row blocks per CTA
+  const long long div = (p.T > 1 && p.T <= kTokGroup) ? 2 : 1;
   if (state_bf16) {
-    const dim3 grid(static_cast<unsigned>(batch * p.h_v * decode_ctas_per_head<__nv_bfloat16>()));
+    const dim3 grid(
+        static_cast<unsigned>(batch * p.h_v * decode_ctas_per_head<__nv_bfloat16>() / div));
     if (p.T > 1)
       gdn_decode_kernel<__nv_bfloat16, true, true><<<grid, kDecodeThreads, 0, st>>>(p);
     else
       gdn_decode_kernel<__nv_bfloat16, false, true><<<grid, kDecodeThreads, 0, st>>>(p);
   } else {
-    const dim3 grid(static_cast<unsigned>(batch * p.h_v * decode_ctas_per_head<float>()));
+    const dim3 grid(static_cast<unsigned>(batch * p.h_v * decode_ctas_per_head<float>() / div));
     if (p.T > 1)
       gdn_decode_kernel<float, true, true><<<grid, kDecodeThreads, 0, st>>>(p);
     else if (p.pool)
