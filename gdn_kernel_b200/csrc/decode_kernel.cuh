@@ -211,8 +211,8 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
   constexpr int kRows = 16 * kRI;   // rows per CTA: 4 warps x 4 rows x kRowIters
   constexpr int kCtasPerHead = kHeadDim / kRows;
   // Multi-token calls of up to kTokGroup tokens give each CTA two consecutive
-  // row blocks: the second block's state streams into shared memory while the
-  // first block's tokens run (decode_pair_blocks).
+  // row blocks (2 x kRows rows of one head): the second block's state streams
+  // into shared memory while the first block's tokens run.
   const bool pair = kMulti && p.T <= kTokGroup;
   const int per_head = pair ? kCtasPerHead / 2 : kCtasPerHead;
   const int bh = blockIdx.x / per_head;   // batch * H_v + v-head

@@ -1,5 +1,6 @@
-"""Sequence-sharded runs on 2 GPUs (one process each) equal the single-GPU run
-bitwise: every CTA of both kernels touches one sequence only."""
+"""Sequence-sharded runs on 2 and 4 GPUs (one process each) equal the single-GPU
+run bitwise: every CTA of both kernels touches one sequence only.  Context-parallel
+prefill at 4 GPUs also exercises the middle ranks (prepare + segment maps)."""
 
 import pytest
 import torch
@@ -10,14 +11,18 @@ from gdn_kernel_b200 import kernel as K, sharding as S, workloads as W
 pytestmark = pytest.mark.gpu
 
 
-def _need_two():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+WORLDS = pytest.mark.parametrize("world", [2, 4])
 
 
-def test_two_gpu_prefill_equals_one_gpu():
-    _need_two()
-    res = S.launch_workers(DW.gpu_prefill_worker, 2, timeout_s=300)
+def _need(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+@WORLDS
+def test_multi_gpu_prefill_equals_one_gpu(world):
+    _need(world)
+    res = S.launch_workers(DW.gpu_prefill_worker, world, timeout_s=300)
     assert all(r.ok for r in res), [r.error for r in res]
     out, ns = res[0].value
     # the workers draw their inputs on the CPU (CPU and CUDA generators differ)
@@ -28,9 +33,10 @@ def test_two_gpu_prefill_equals_one_gpu():
     assert torch.equal(out, ro.cpu()) and torch.equal(ns, rs.cpu())
 
 
-def test_two_gpu_decode_equals_one_gpu():
-    _need_two()
-    res = S.launch_workers(DW.gpu_decode_worker, 2, timeout_s=300)
+@WORLDS
+def test_multi_gpu_decode_equals_one_gpu(world):
+    _need(world)
+    res = S.launch_workers(DW.gpu_decode_worker, world, timeout_s=300)
     assert all(r.ok for r in res), [r.error for r in res]
     outs, state = res[0].value
     first, tokens = W.make_decode_run(DW.DECODE_BATCH, 3, seed=12, h_qk=2, h_v=4)
@@ -43,13 +49,14 @@ def test_two_gpu_decode_equals_one_gpu():
     assert torch.equal(outs, torch.stack(ref)) and torch.equal(state, st.cpu())
 
 
-def test_two_gpu_context_parallel_prefill():
-    """One 333-token sequence split over 2 GPUs (NCCL all-gather of the segment
-    maps) against the fp32 oracle of the whole sequence."""
-    _need_two()
+@WORLDS
+def test_multi_gpu_context_parallel_prefill(world):
+    """One 333-token sequence split over 2 or 4 GPUs (NCCL all-gather of the
+    segment maps) against the fp32 oracle of the whole sequence."""
+    _need(world)
     from helpers import assert_prefill_close
     from oracle import gdn_oracle as O
-    res = S.launch_workers(DW.gpu_cp_worker, 2, backend="nccl", timeout_s=300)
+    res = S.launch_workers(DW.gpu_cp_worker, world, backend="nccl", timeout_s=300)
     assert all(r.ok for r in res), [r.error for r in res]
     out, end = res[0].value
     x = DW._cp_inputs()
