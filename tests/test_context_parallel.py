@@ -35,7 +35,7 @@ def test_segment_affine_map_is_exact():
         torch.testing.assert_close(s0 @ m + n, ref[0], atol=2e-5, rtol=1e-4)
 
 
-@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_cp_protocol_over_gloo_equals_whole_sequence(world):
     res = S.launch_workers(DW.cp_worker, world, timeout_s=300)
     assert all(r.ok for r in res), [r.error for r in res]

@@ -1,6 +1,8 @@
-"""Sequence-sharded runs on 2 and 4 GPUs (one process each) equal the single-GPU
+"""Sequence-sharded runs on 2, 4 and 8 GPUs (one process each) equal the single-GPU
 run bitwise: every CTA of both kernels touches one sequence only.  Context-parallel
-prefill at 4 GPUs also exercises the middle ranks (prepare + segment maps)."""
+prefill at 4 GPUs also exercises the middle ranks (prepare + segment maps); at 8 the
+333-token sequence leaves three ranks with empty segments (identity maps) and the
+5-entry decode batch leaves three ranks with no entries."""
 
 import pytest
 import torch
@@ -11,7 +13,7 @@ from gdn_kernel_b200 import kernel as K, sharding as S, workloads as W
 pytestmark = pytest.mark.gpu
 
 
-WORLDS = pytest.mark.parametrize("world", [2, 4])
+WORLDS = pytest.mark.parametrize("world", [2, 4, 8])
 
 
 def _need(world):
@@ -51,7 +53,7 @@ def test_multi_gpu_decode_equals_one_gpu(world):
 
 @WORLDS
 def test_multi_gpu_context_parallel_prefill(world):
-    """One 333-token sequence split over 2 or 4 GPUs (NCCL all-gather of the
+    """One 333-token sequence split over 2, 4 or 8 GPUs (NCCL all-gather of the
     segment maps) against the fp32 oracle of the whole sequence."""
     _need(world)
     from helpers import assert_prefill_close
