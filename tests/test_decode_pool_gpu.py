@@ -96,6 +96,26 @@ def test_bf16_state_pool(T):
     torch.testing.assert_close(inter.float(), ri.float(), **BF16_STATE_TOL)
 
 
+@pytest.mark.parametrize("state_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T", [2, 16])   # both ends of the two-row-blocks-per-CTA path
+def test_multi_token_padding_and_write_slots(T, state_dtype):
+    """T > 1 with a padding entry (read index -1) and separate write slots: the
+    padding entry's outputs are zero on every row of both row blocks a CTA
+    owns (the output buffer starts as NaN), and no slot but the written ones
+    changes."""
+    x = W.make_pool_decode_inputs(4, T, 10, seed=70 + T, state_dtype=state_dtype)
+    read = torch.tensor([6, -1, 0, 9], dtype=torch.int32)
+    write = torch.tensor([1, 8, 2, 7], dtype=torch.int32)   # no slot both read and written
+    out, pool, _ = _run(x, read, write=write)
+    ro, rp, _ = _oracle(x, read, write=write)
+    tol = DECODE_STATE_TOL if state_dtype == torch.float32 else BF16_STATE_TOL
+    torch.testing.assert_close(out.float(), ro.float(), **DECODE_OUT_TOL)
+    assert torch.equal(out[1].float(), torch.zeros_like(out[1].float()))
+    torch.testing.assert_close(pool.float(), rp.float(), **tol)
+    for s in (0, 3, 4, 5, 6, 8, 9):   # read-only, untouched or the padding entry's slot
+        assert torch.equal(pool[s], x.pool[s])
+
+
 def test_in_place_equals_out_of_place():
     x = W.make_pool_decode_inputs(4, 3, 4, seed=40)
     o1, p1, _ = _run(x, x.indices, in_place=True)
