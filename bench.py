@@ -20,8 +20,9 @@ Also reported on the same line:
   host-to-device inputs and device-to-host output inside the timed region;
 * ``clocks``: nvidia-smi samples taken during the measurements.
 
-``--profile decode|prefill`` only launches a few kernels of one case (no timing,
-no output line): the command that the ncu summaries under profiles/ were made with.
+``--profile decode|decode_pool|prefill`` only launches a few kernels of one case (no
+timing, no output line): the command that the ncu summaries under profiles/ were made
+with.
 
 ``--impl reference`` times the reference's algorithm on the host cores
 (the fp32 CPU restatement in oracle/, rank 0 only) for the same metric.
@@ -580,6 +581,14 @@ def run_profile(args):
         for _ in range(args.launches):
             K.gdn_decode(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.scale, out,
                          x.state)
+    elif args.profile == "decode_pool":
+        sdt = torch.bfloat16 if args.pool_dtype == "bf16" else torch.float32
+        x = W.make_pool_decode_inputs(args.batch, args.seq_len, 2 * args.batch, seed=7000,
+                                      device="cuda", state_dtype=sdt)
+        out = torch.empty(args.batch, args.seq_len, H_V, D, dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.launches):
+            K.gdn_decode_pool(x.q, x.k, x.v, x.pool, x.indices, x.A_log, x.a, x.dt_bias, x.b,
+                              x.scale, out)
     else:
         lengths = ([args.tokens] if args.sequences == 1
                    else W.varlen_lengths(args.sequences, 128, args.tokens, seed=3))
@@ -603,7 +612,10 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=20)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true", help="headline decode + e2e only")
-    ap.add_argument("--profile", choices=["decode", "prefill"], default=None)
+    ap.add_argument("--profile", choices=["decode", "decode_pool", "prefill"], default=None)
+    ap.add_argument("--seq-len", type=int, default=4, help="--profile decode_pool: tokens per entry")
+    ap.add_argument("--pool-dtype", choices=["fp32", "bf16"], default="fp32",
+                    help="--profile decode_pool: state pool type")
     ap.add_argument("--launches", type=int, default=4)
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--sequences", type=int, default=1)

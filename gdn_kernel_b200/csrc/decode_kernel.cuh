@@ -375,28 +375,55 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
     qk += __shfl_xor_sync(0xffffffffu, qk, 4);
 #pragma unroll
     for (int i = 0; i < kRI; ++i) {
+      if constexpr (kMulti) {
+        // Several tokens run back to back on the state in registers, so this
+        // product is on the path from one token to the next: four short
+        // chains instead of one of 16.  The steps are issue-bound, so the
+        // element-wise work runs as packed pairs (sm_100 f32x2 multiply and
+        // fma, each lane rounded exactly as the scalar instruction): the
+        // decay, the chains (accumulators 0-1 and 2-3 as pairs) and the update.
+        const float2 g2 = make_float2(g, g);
+        float2 s2[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+          s2[m] = __fmul2_rn(g2, make_float2(st[i][2 * m], st[i][2 * m + 1]));
+        float2 ak01 = make_float2(0.f, 0.f), ak23 = ak01, aq01 = ak01, aq23 = ak01;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int e = 4 * m;
+          ak01 = __ffma2_rn(s2[2 * m], make_float2(kf[e], kf[e + 1]), ak01);
+          ak23 = __ffma2_rn(s2[2 * m + 1], make_float2(kf[e + 2], kf[e + 3]), ak23);
+          aq01 = __ffma2_rn(s2[2 * m], make_float2(qf[e], qf[e + 1]), aq01);
+          aq23 = __ffma2_rn(s2[2 * m + 1], make_float2(qf[e + 2], qf[e + 3]), aq23);
+        }
+        float dk = (ak01.x + ak01.y) + (ak23.x + ak23.y);
+        float dq = (aq01.x + aq01.y) + (aq23.x + aq23.y);
+#pragma unroll
+        for (int m = 1; m < 8; m <<= 1) {
+          dk += __shfl_xor_sync(0xffffffffu, dk, m);
+          dq += __shfl_xor_sync(0xffffffffu, dq, m);
+        }
+        const float delta = beta * (vv[i] - dk);
+        const float2 d2 = make_float2(delta, delta);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const float2 u = __ffma2_rn(d2, make_float2(kf[2 * m], kf[2 * m + 1]), s2[m]);
+          st[i][2 * m] = u.x;
+          st[i][2 * m + 1] = u.y;
+        }
+        if (l8 == 0)
+          p.out[(tok * p.h_v + h) * kHeadDim + row0 + 4 * i] =
+              __float2bfloat16(p.scale * (dq + delta * qk));
+        continue;
+      }
       float s[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) s[e] = g * st[i][e];
       float dk = 0.f, dq = 0.f;
-      if constexpr (kMulti) {
-        // Several tokens run back to back on the state in registers, so this
-        // product is on the path from one token to the next: four short
-        // chains instead of one of 16.
-        float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          ak[e & 3] = fmaf(s[e], kf[e], ak[e & 3]);
-          aq[e & 3] = fmaf(s[e], qf[e], aq[e & 3]);
-        }
-        dk = (ak[0] + ak[1]) + (ak[2] + ak[3]);
-        dq = (aq[0] + aq[1]) + (aq[2] + aq[3]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          dk = fmaf(s[e], kf[e], dk);
-          dq = fmaf(s[e], qf[e], dq);
-        }
+      for (int e = 0; e < 16; ++e) {
+        dk = fmaf(s[e], kf[e], dk);
+        dq = fmaf(s[e], qf[e], dq);
       }
 #pragma unroll
       for (int m = 1; m < 8; m <<= 1) {
