@@ -364,15 +364,19 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
     beta = 1.0f / (1.0f + expf(-bv));
   };
   // One token step on this thread's rows (inputs already unpacked, gates formed).
+  // (The multi-token instance passes q.k in, formed once per staged token.)
   auto step = [&](int t, const float* qf, const float* kf, float g, float beta,
-                  const float* vv) {
+                  const float* vv, float qk_pre) {
     const size_t tok = static_cast<size_t>(bidx) * p.T + t;
-    float qk = 0.f;
+    float qk = qk_pre;
+    if constexpr (!kMulti) {
+      qk = 0.f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) qk = fmaf(qf[e], kf[e], qk);
-    qk += __shfl_xor_sync(0xffffffffu, qk, 1);
-    qk += __shfl_xor_sync(0xffffffffu, qk, 2);
-    qk += __shfl_xor_sync(0xffffffffu, qk, 4);
+      for (int e = 0; e < 16; ++e) qk = fmaf(qf[e], kf[e], qk);
+      qk += __shfl_xor_sync(0xffffffffu, qk, 1);
+      qk += __shfl_xor_sync(0xffffffffu, qk, 2);
+      qk += __shfl_xor_sync(0xffffffffu, qk, 4);
+    }
 #pragma unroll
     for (int i = 0; i < kRI; ++i) {
       if constexpr (kMulti) {
@@ -456,7 +460,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
     for (int i = 0; i < kRI; ++i) vv[i] = __bfloat162float(cur.v[i]);
     float g, beta;
     gates(__bfloat162float(cur.a), __bfloat162float(cur.b), g, beta);
-    step(0, qf, kf, g, beta, vv);
+    step(0, qf, kf, g, beta, vv, 0.f);
   } else {
     // Staged token inputs: q and k rows (256 B each), a, b, and this CTA's v rows.
     __shared__ __align__(16) __nv_bfloat16 sq[kTokGroup][kHeadDim];
@@ -464,37 +468,43 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
     __shared__ float sa[kTokGroup], sb[kTokGroup];
     __shared__ __align__(16) __nv_bfloat16 sv[kTokGroup][2 * kRows];
     __shared__ __align__(16) StateT sst[kRows][kHeadDim];   // the second row block's state
+    // q.k of each staged token, per warp (written and read by the same warp).
+    __shared__ float sqk[kDecodeThreads / 32][kTokGroup];
     const int tid = threadIdx.x;
     const int vrows = pair ? 2 * kRows : kRows;
+    // This lane's 16 columns of staged token tt's q and k, as floats.
+    auto load_qk = [&](int tt, float* qf, float* kf) {
+#pragma unroll
+      for (int j = 0; j < kAcc; ++j) {
+        uint32_t wq[kVec / 2], wk[kVec / 2];
+        if constexpr (kVec == 4) {
+          const uint2 uq = *reinterpret_cast<const uint2*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
+          const uint2 uk = *reinterpret_cast<const uint2*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
+          wq[0] = uq.x; wq[1] = uq.y; wk[0] = uk.x; wk[1] = uk.y;
+        } else {
+          const uint4 uq = *reinterpret_cast<const uint4*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
+          const uint4 uk = *reinterpret_cast<const uint4*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
+          wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
+          wk[0] = uk.x; wk[1] = uk.y; wk[2] = uk.z; wk[3] = uk.w;
+        }
+#pragma unroll
+        for (int w = 0; w < kVec / 2; ++w) {
+          const float2 fq = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wq[w]));
+          const float2 fk = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wk[w]));
+          qf[kVec * j + 2 * w] = fq.x; qf[kVec * j + 2 * w + 1] = fq.y;
+          kf[kVec * j + 2 * w] = fk.x; kf[kVec * j + 2 * w + 1] = fk.y;
+        }
+      }
+    };
     // One staged token group's steps on this thread's rows.
     auto run_tokens = [&](int t0, int n) {
         for (int tt = 0; tt < n; ++tt) {
           float qf[16], kf[16], vv[kRI];
-#pragma unroll
-          for (int j = 0; j < kAcc; ++j) {
-            uint32_t wq[kVec / 2], wk[kVec / 2];
-            if constexpr (kVec == 4) {
-              const uint2 uq = *reinterpret_cast<const uint2*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
-              const uint2 uk = *reinterpret_cast<const uint2*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
-              wq[0] = uq.x; wq[1] = uq.y; wk[0] = uk.x; wk[1] = uk.y;
-            } else {
-              const uint4 uq = *reinterpret_cast<const uint4*>(&sq[tt][kVec * l8 + 8 * kVec * j]);
-              const uint4 uk = *reinterpret_cast<const uint4*>(&sk[tt][kVec * l8 + 8 * kVec * j]);
-              wq[0] = uq.x; wq[1] = uq.y; wq[2] = uq.z; wq[3] = uq.w;
-              wk[0] = uk.x; wk[1] = uk.y; wk[2] = uk.z; wk[3] = uk.w;
-            }
-#pragma unroll
-            for (int w = 0; w < kVec / 2; ++w) {
-              const float2 fq = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wq[w]));
-              const float2 fk = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&wk[w]));
-              qf[kVec * j + 2 * w] = fq.x; qf[kVec * j + 2 * w + 1] = fq.y;
-              kf[kVec * j + 2 * w] = fk.x; kf[kVec * j + 2 * w + 1] = fk.y;
-            }
-          }
+          load_qk(tt, qf, kf);
 #pragma unroll
           for (int i = 0; i < kRI; ++i)
             vv[i] = __bfloat162float(sv[tt][row0 - rblk * kRows + 4 * i]);
-          step(t0 + tt, qf, kf, sa[tt], sb[tt], vv);
+          step(t0 + tt, qf, kf, sa[tt], sb[tt], vv, sqk[warp][tt]);
         }
     };
     for (int t0 = 0; t0 < p.T; t0 += kTokGroup) {
@@ -541,6 +551,24 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
       // the group's gates, formed once for all rows (sa = g, sb = beta)
       if (tid < n) gates(ga, gb, sa[tid], sb[tid]);
       __syncthreads();
+      // q.k of the group's tokens once per warp, not once per token step and
+      // row block: four tokens per pass, eight lanes each, over the columns
+      // and the xor tree a token step uses, so the sums are the same bits.
+      for (int p0 = 0; p0 < n; p0 += 4) {
+        const int tt = p0 + (lane >> 3);
+        float part = 0.f;
+        if (tt < n) {
+          float qf[16], kf[16];
+          load_qk(tt, qf, kf);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) part = fmaf(qf[e], kf[e], part);
+        }
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+        part += __shfl_xor_sync(0xffffffffu, part, 4);
+        if (tt < n && l8 == 0) sqk[warp][tt] = part;
+      }
+      __syncwarp();
       run_tokens(t0, n);
     }
     if (pair) {
