@@ -362,6 +362,7 @@ SplitParams split_params(const PrefillParams& p, void* workspace, const SplitLay
   sp.max_chunks = static_cast<int>(L.max_chunks);
   sp.c_lo = 0;
   sp.c_hi = std::numeric_limits<int>::max();
+  sp.wait_table = 0;
   return sp;
 }
 
@@ -397,13 +398,23 @@ void launch_prep(const SplitParams& sp, const CUtensorMap& tq, const CUtensorMap
   }
 }
 
+// The prep grid that follows the chunk-table kernel is launched with
+// programmatic serialization and waits for the table inside (wait_table), so
+// its launch and setup overlap the table kernel.
+void launch_table_then_prep(const SplitParams& sp, const CUtensorMap& tq, const CUtensorMap& tk,
+                            long long items, long long max_ctas, cudaStream_t st) {
+  gdn_chunk_table_kernel<<<1, kTableThreads, 0, st>>>(sp);
+  SplitParams first = sp;
+  first.wait_table = 1;
+  launch_prep(first, tq, tk, items, max_ctas, true, st);
+}
+
 // Chunk table and per-(chunk, v-head) records into the workspace.
 void launch_prepare(const SplitParams& sp, const CUtensorMap& tq, const CUtensorMap& tk,
                     const SplitLayout& L, int32_t num_v_heads, cudaStream_t st) {
-  gdn_chunk_table_kernel<<<1, kTableThreads, 0, st>>>(sp);
   // Persistent: two CTAs per SM (at most one per item) walk the items.
-  launch_prep(sp, tq, tk, L.max_chunks * static_cast<long long>(num_v_heads),
-              2LL * device_sm_count(), false, st);
+  launch_table_then_prep(sp, tq, tk, L.max_chunks * static_cast<long long>(num_v_heads),
+                         2LL * device_sm_count(), st);
 }
 
 // The state recurrence over a prepared workspace (reads it only).  A chain
@@ -460,7 +471,6 @@ void launch_two_stage(const SplitParams& sp, const CUtensorMap& tq, const CUtens
     launch_recur(sp, tk, tv, num_seqs, num_v_heads, st);
     return;
   }
-  gdn_chunk_table_kernel<<<1, kTableThreads, 0, st>>>(sp);
   const int count = static_cast<int>(
       std::max<long long>(2, std::min<long long>(kPieceMaxCount, nch / kPieceChunksPer)));
   // piece i ends after a share (1 - r^{i+1}) / (1 - r^count) of the chunks
@@ -476,7 +486,7 @@ void launch_two_stage(const SplitParams& sp, const CUtensorMap& tq, const CUtens
     if (i > 0) piece.base.state = sp.base.new_state;   // where the previous piece ended
     const long long items = (std::min<long long>(hi, nch) - lo) * num_v_heads;
     if (i == 0)
-      launch_prep(piece, tq, tk, items, 2LL * sms, false, st);
+      launch_table_then_prep(piece, tq, tk, items, 2LL * sms, st);
     else
       launch_prep(piece, tq, tk, items, 2LL * (sms - chain_ctas), true, st);
     launch_recur(piece, tk, tv, num_seqs, num_v_heads, st);

@@ -75,6 +75,9 @@ struct SplitParams {
   uint8_t* records;       // [max_chunks][H_v] x kRecBytes
   int num_seqs;
   int max_chunks;
+  // Prep kernel: launched to follow the chunk-table kernel (programmatic
+  // serialization), so it waits for that grid before reading the table.
+  int wait_table;
   // Chunk window [c_lo, c_hi): the prep kernel does the items of table chunks
   // in it, the chain kernel the chunks of each sequence in it (index within
   // the sequence).  The whole call is [0, INT_MAX); a one-sequence call split
@@ -99,6 +102,9 @@ constexpr int kTableThreads = 1024;
 __global__ void __launch_bounds__(kTableThreads) gdn_chunk_table_kernel(SplitParams sp) {
   __shared__ int warp_sums[32];
   __shared__ int carry_s;
+  // The prep grid after this one may start its setup now (it waits for this
+  // grid's completion before it reads the table).
+  pdl_launch_dependents();
   const PrefillParams& p = sp.base;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) carry_s = 0;
@@ -226,7 +232,6 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   const PrefillParams& p = sp.base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2, row = quad * 32 + lane;
-  const int n_chunks = min(sp.header[0], sp.c_hi);
 
   // One mbarrier per product, each completing once per item (phase parity =
   // item parity j & 1).  Warps wait on them without a CTA-wide barrier in
@@ -272,6 +277,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
   const uint32_t tmem = *tmem_ptr;
   const uint32_t tm_lane = static_cast<uint32_t>(quad * 32) << 16;
   const uint32_t a_tpzt = smem_u32(tpzt);
+  // The first prep of a call is launched to follow the chunk-table kernel and
+  // may start before the table is complete: the setup above reads nothing the
+  // table kernel writes, and the wait here precedes every table read.
+  if (sp.wait_table) pdl_wait();
+  const int n_chunks = min(sp.header[0], sp.c_hi);
 
   // Items are (chunk, v-head) pairs in chunk-major order; a CTA steps through
   // them gridDim.x at a time, i.e. by (dc chunks, dh heads), without dividing.
