@@ -418,28 +418,28 @@ __global__ void __launch_bounds__(kDecodeThreads, (!kMulti && sizeof(StateT) == 
         if (l8 == 0)
           p.out[(tok * p.h_v + h) * kHeadDim + row0 + 4 * i] =
               __float2bfloat16(p.scale * (dq + delta * qk));
-        continue;
+      } else {
+        float s[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) s[e] = g * st[i][e];
+        float dk = 0.f, dq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          dk = fmaf(s[e], kf[e], dk);
+          dq = fmaf(s[e], qf[e], dq);
+        }
+#pragma unroll
+        for (int m = 1; m < 8; m <<= 1) {
+          dk += __shfl_xor_sync(0xffffffffu, dk, m);
+          dq += __shfl_xor_sync(0xffffffffu, dq, m);
+        }
+        const float delta = beta * (vv[i] - dk);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) st[i][e] = fmaf(delta, kf[e], s[e]);
+        if (l8 == 0)
+          p.out[(tok * p.h_v + h) * kHeadDim + row0 + 4 * i] =
+              __float2bfloat16(p.scale * (dq + delta * qk));
       }
-      float s[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) s[e] = g * st[i][e];
-      float dk = 0.f, dq = 0.f;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        dk = fmaf(s[e], kf[e], dk);
-        dq = fmaf(s[e], qf[e], dq);
-      }
-#pragma unroll
-      for (int m = 1; m < 8; m <<= 1) {
-        dk += __shfl_xor_sync(0xffffffffu, dk, m);
-        dq += __shfl_xor_sync(0xffffffffu, dq, m);
-      }
-      const float delta = beta * (vv[i] - dk);
-#pragma unroll
-      for (int e = 0; e < 16; ++e) st[i][e] = fmaf(delta, kf[e], s[e]);
-      if (l8 == 0)
-        p.out[(tok * p.h_v + h) * kHeadDim + row0 + 4 * i] =
-            __float2bfloat16(p.scale * (dq + delta * qk));
     }
     if (p.inter) {   // state after token t, at [read slot, t]
       StateT* dst = static_cast<StateT*>(p.inter) + ((ridx * p.T + t) * p.h_v + h) * hd2 +
