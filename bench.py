@@ -37,7 +37,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -71,13 +70,76 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name):
-    """DRAM bytes per launch recorded by an ncu capture summarised in profiles/."""
-    path = os.path.join(ROOT, "profiles", name)
-    if not os.path.exists(path):
+NCU_METRICS = "dram__bytes_read.sum,dram__bytes_write.sum,lts__t_sectors_op_write.sum"
+
+
+def _ncu_rows(csv_path):
+    """(kernel name, metric name, value) rows of an ncu --csv log."""
+    import csv
+    rows = []
+    with open(csv_path, newline="") as f:
+        lines = [ln for ln in f if ln.startswith('"')]
+    for rec in csv.DictReader(lines):
+        try:
+            val = float(str(rec.get("Metric Value", "")).replace(",", ""))
+        except ValueError:
+            continue
+        rows.append((rec.get("Kernel Name", ""), rec.get("Metric Name", ""),
+                     val * {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(
+                         rec.get("Metric Unit", "byte"), 1.0), rec.get("ID", "")))
+    return rows
+
+
+def measure_traffic(profile_args, kernel_regex, skip, count, cache_control, timeout_s=600):
+    """DRAM traffic of the kernels of one small invocation, from one ncu capture
+    of this file's --profile mode (run as a child process before this process
+    touches the GPU).  Writes are counted where they enter L2
+    (lts__t_sectors_op_write x 32 B): a kernel's dirty lines reach DRAM after its
+    window closes (when the next kernel evicts them), so dram__bytes_write.sum
+    alone undercounts them.  Reads are dram__bytes_read.sum.  Returns per-launch
+    totals summed over the captured kernels, or None when ncu is unavailable."""
+    import shutil
+    import tempfile
+    ncu = shutil.which("ncu")
+    if ncu is None:
         return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
-    return float(m.group(1)) if m else None
+    with tempfile.TemporaryDirectory() as td:
+        log_path = os.path.join(td, "traffic.csv")
+        cmd = [ncu, "--metrics", NCU_METRICS, "--clock-control", "none",
+               "--cache-control", cache_control, "-k", f"regex:{kernel_regex}", "-s", str(skip),
+               "-c", str(count), "--csv", "--print-units", "base", "--log-file", log_path,
+               sys.executable,
+               os.path.abspath(__file__), "--profile", *profile_args]
+        try:
+            res = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
+                                 timeout=timeout_s)
+        except (OSError, subprocess.TimeoutExpired) as e:
+            log(f"traffic capture failed: {e}")
+            return None
+        if res.returncode != 0 or not os.path.exists(log_path):
+            log(f"traffic capture failed (rc={res.returncode}): {res.stdout[-2000:]}")
+            return None
+        rows = _ncu_rows(log_path)
+    if not rows:
+        return None
+    tot = {"dram_read": 0.0, "dram_write_in_window": 0.0, "l2_write": 0.0}
+    kernels = {}
+    for kname, metric, val, kid in rows:
+        key = {"dram__bytes_read.sum": "dram_read", "dram__bytes_write.sum": "dram_write_in_window",
+               "lts__t_sectors_op_write.sum": "l2_write"}.get(metric)
+        if key is None:
+            continue
+        if key == "l2_write":
+            val *= 32.0
+        tot[key] += val
+        kernels.setdefault(kname.split("(")[0].split("<")[0], set()).add(kid)
+    tot["bytes"] = tot["dram_read"] + max(tot["l2_write"], tot["dram_write_in_window"])
+    tot["launches"] = {k: len(v) for k, v in kernels.items()}
+    tot["command"] = " ".join(["ncu", "--metrics", NCU_METRICS, "--clock-control", "none",
+                               "--cache-control", cache_control, "-k", f"regex:{kernel_regex}",
+                               "-s", str(skip), "-c", str(count), "python bench.py --profile",
+                               *profile_args])
+    return tot
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -279,6 +341,185 @@ def time_prefill(K, lengths, iters, warmup, flush, seed=0, with_state=True):
     return [e0.elapsed_time(e1) for e0, e1 in ev]
 
 
+def prefill_case(K, lengths, with_state, seed, iters, warmup, flush, prefix_curve=0):
+    """Times the default prefill (two-stage path, workspace allocated outside the
+    timed region) on configs-shaped inputs and keeps what the drift report needs
+    on the host: the inputs, the outputs and, with ``prefix_curve`` > 0 (one
+    sequence), the final state of the prefixes of prefix_curve, 2 prefix_curve, ...
+    tokens run as their own calls."""
+    from gdn_kernel_b200 import workloads as W
+
+    x = W.make_prefill_inputs(lengths, seed=seed, device="cuda", with_state=with_state)
+    T, N = sum(lengths), len(lengths)
+    out = torch.empty(T, H_V, D, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(N, H_V, D, D, dtype=torch.float32, device="cuda")
+    ws = torch.empty(K.prefill_workspace_bytes(N, T, H_V), dtype=torch.uint8, device="cuda")
+    args = (x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale, out, ns)
+    for _ in range(warmup):
+        flush.zero_()
+        K.gdn_prefill(*args, workspace=ws)
+    torch.cuda.synchronize()
+    ev = [_events() for _ in range(iters)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        K.gdn_prefill(*args, workspace=ws)
+        e1.record()
+    torch.cuda.synchronize()
+    times = [e0.elapsed_time(e1) for e0, e1 in ev]
+    prefix_states = []
+    if prefix_curve and N == 1:
+        for n in range(prefix_curve, T + 1, prefix_curve):
+            cu = torch.tensor([0, n], dtype=x.cu_seqlens.dtype, device="cuda")
+            o_p, s_p = K.prefill(x.q[:n], x.k[:n], x.v[:n], x.state, x.A_log, x.a[:n],
+                                 x.dt_bias, x.b[:n], cu, x.scale)
+            prefix_states.append((n, s_p.cpu()))
+    host = {n: (getattr(x, n).cpu() if getattr(x, n) is not None else None)
+            for n in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens")}
+    host["scale"] = x.scale
+    res = {"times": times, "inputs": host, "out": out.cpu(), "new_state": ns.cpu(),
+           "prefix_states": prefix_states, "gpu_inputs": x}
+    return res
+
+
+def prefill_drift_and_cpu(case, lengths):
+    """The fp32 CPU oracle (chunked restatement of the reference prefill) on all
+    host cores: its throughput is the CPU baseline of the case, and its results
+    measure the GPU path's drift: output error, final-state relative Frobenius
+    error per (sequence, head), and for one sequence the same error of the state
+    after every prefix of the drift curve."""
+    from oracle import gdn_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x = case["inputs"]
+    t0 = time.perf_counter()
+    ro, rs, chunk_states = O.prefill_chunked(x["q"], x["k"], x["v"], x["state"], x["A_log"],
+                                             x["a"], x["dt_bias"], x["b"], x["cu_seqlens"],
+                                             x["scale"], return_chunk_states=True)
+    sec = time.perf_counter() - t0
+    T = sum(lengths)
+
+    def relfro(a, b):
+        a, b = a.double(), b.double()
+        return ((a - b).flatten(-2).norm(dim=-1) / b.flatten(-2).norm(dim=-1).clamp_min(1e-30))
+
+    err = (case["out"].float() - ro.float()).abs()
+    sr = relfro(case["new_state"], rs)                                   # [N, H_v]
+    drift = {"out_max_abs": float(err.max()), "out_mean_abs": float(err.mean()),
+             "state_relfro_max": float(sr.max()), "state_relfro_mean": float(sr.mean()),
+             "per_sequence_state_relfro_max": [round(float(v), 6) for v in sr.max(dim=1).values],
+             "tolerance": "output atol = rtol = 2e-2; final state relative Frobenius <= 1e-2 "
+                          "per (sequence, head)",
+             "reference": "oracle.gdn_oracle.prefill_chunked (fp32 CPU)"}
+    if case["prefix_states"]:
+        curve = []
+        cs = chunk_states[0]
+        for n, st in case["prefix_states"]:
+            ref = rs[0] if n >= T else cs[n // 64]
+            w0 = max(0, n - case["prefix_states"][0][0])
+            curve.append({"tokens": n,
+                          "state_relfro_max": round(float(relfro(st[0], ref).max()), 6),
+                          "out_max_abs_window": round(float(err[w0:n].max()), 6)})
+        drift["curve"] = curve
+    cpu = {"value": round(T / sec, 1), "unit": "tokens/s", "cores": os.cpu_count(),
+           "kind": "port",
+           "sample": f"the whole case ({T} tokens, {len(lengths)} sequences) through the fp32 "
+                     f"chunked CPU oracle (torch, {torch.get_num_threads()} threads): "
+                     f"{sec:.2f} s"}
+    return drift, cpu, ro
+
+
+def flashinfer_prefill(case, lengths, iters, warmup, flush):
+    """FlashInfer's Blackwell chunked GDN prefill (CuTe-DSL tcgen05 kernel,
+    flashinfer.gdn_kernels.blackwell) on the same inputs, timed the same way: a
+    reference point only, never on this package's path.  Its gate input is the
+    per-token decay g = exp(log g) and beta = sigmoid(b), both fp32 (formed once,
+    outside the timed region)."""
+    try:
+        from flashinfer.gdn_kernels import _has_blackwell_prefill, chunk_gated_delta_rule_sm100
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer import failed: {e!r}"[:300]}
+    if not _has_blackwell_prefill:
+        return {"unavailable": "flashinfer reports no Blackwell prefill kernel"}
+    import torch.nn.functional as F
+
+    x = case["gpu_inputs"]
+    xa = x.a.float() + x.dt_bias.float()
+    gate = torch.exp(-torch.exp(x.A_log.float()) * F.softplus(xa, beta=1.0, threshold=20.0))
+    gate = gate.contiguous()
+    beta = torch.sigmoid(x.b.float()).contiguous()
+    T, N = sum(lengths), len(lengths)
+    out = torch.empty(T, H_V, D, dtype=torch.bfloat16, device="cuda")
+    ost = torch.empty(N, H_V, D, D, dtype=torch.float32, device="cuda")
+    cu32 = x.cu_seqlens.to(torch.int32)
+
+    def run():
+        chunk_gated_delta_rule_sm100(x.q, x.k, x.v, gate, beta, out, cu32, x.state, ost, x.scale)
+    try:
+        t0 = time.perf_counter()
+        run()
+        torch.cuda.synchronize()
+        first_s = time.perf_counter() - t0
+        for _ in range(warmup):
+            flush.zero_()
+            run()
+        torch.cuda.synchronize()
+        ev = [_events() for _ in range(iters)]
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record()
+            run()
+            e1.record()
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer run failed: {e!r}"[:300]}
+    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
+    return {"us": round(ms * 1e3, 1), "tokens_per_s": round(T / (ms * 1e-3), 1),
+            "first_call_s": round(first_s, 1), "out": out.cpu(), "new_state": ost.cpu(),
+            "kernel": "flashinfer.gdn_kernels.chunk_gated_delta_rule_sm100 "
+                      "(flashinfer 0.6.11.post2, CuTe DSL, sm_100)"}
+
+
+def flashinfer_decode(batch, iters, warmup, flush, state_dtype, seed=0):
+    """FlashInfer's pretranspose GDN decode (k-last state [B, H_v, V, K], in place,
+    no in-kernel q/k normalisation) at the headline shape, timed like our decode:
+    fp32 state takes its legacy T=1 kernel, bf16 state its BF16-state kernel."""
+    from gdn_kernel_b200 import workloads as W
+
+    try:
+        from flashinfer.gdn_decode import gated_delta_rule_decode_pretranspose
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer import failed: {e!r}"[:300]}
+    x = W.make_decode_inputs(batch, seed=seed, device="cuda")
+    state = x.state.to(state_dtype).contiguous()
+    out = torch.empty(batch, 1, H_V, D, dtype=torch.bfloat16, device="cuda")
+
+    def run():
+        gated_delta_rule_decode_pretranspose(x.q, x.k, x.v, state, x.A_log, x.a, x.dt_bias, x.b,
+                                             x.scale, out, use_qk_l2norm=False)
+    try:
+        run()
+        for _ in range(warmup):
+            flush.zero_()
+            run()
+        torch.cuda.synchronize()
+        ev = [_events() for _ in range(iters)]
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record()
+            run()
+            e1.record()
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer run failed: {e!r}"[:300]}
+    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
+    esz = 4 if state_dtype == torch.float32 else 2
+    nbytes = batch * H_V * D * D * esz * 2
+    return {"us": round(ms * 1e3, 2), "state_GBps": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "kernel": "flashinfer.gdn_decode.gated_delta_rule_decode_pretranspose "
+                      f"({'fp32' if esz == 4 else 'bf16'} state, use_qk_l2norm=False)"}
+
+
 def _max_over_ranks(ms, world):
     if world == 1:
         return ms
@@ -400,7 +641,7 @@ def cpu_decode_sample(batch, steps, seed=0):
     return (time.perf_counter() - t0) / steps
 
 
-def run_gpu(args, rank, world, local_rank):
+def run_gpu(args, rank, world, local_rank, traffic=None):
     import torch.distributed as dist
 
     from gdn_kernel_b200 import _lib, kernel as K
@@ -476,12 +717,13 @@ def run_gpu(args, rank, world, local_rank):
         extra["decode_pool"] = pool
         # ---- prefill configs[2] and configs[3]
         from gdn_kernel_b200 import workloads as W
-        pre = {}
+        pre, cases = {}, {}
         for name, lengths, with_state in (
                 ("T8192", [8192], False),
                 ("varlen16", W.varlen_lengths(16, 128, 8192, seed=3), True)):
-            ts = time_prefill(K, lengths, 5, 2, flush, seed=4000 + rank, with_state=with_state)
-            ms = statistics.median(ts)
+            case = prefill_case(K, lengths, with_state, 4000 + rank, 5, 2, flush,
+                                prefix_curve=1024 if len(lengths) == 1 else 0)
+            ms = statistics.median(case["times"])
             T = sum(lengths)
             flop = T * H_V * PREFILL_FLOP_PER_TOKEN_HEAD
             hb = prefill_hbm_bytes(lengths, with_state)
@@ -493,13 +735,44 @@ def run_gpu(args, rank, world, local_rank):
                 "hbm_GBps": round(hb / (ms * 1e-3) / 1e9, 1),
                 "hbm_frac": round(hb / (ms * 1e-3) / 1e9 / hbm_peak, 4),
                 "algorithmic_flop": flop, "algorithmic_bytes": hb,
+                "path": "gdn_prefill (two-stage kernels, caller workspace)",
             }
+            if world == 1 and rank == 0 and not args.no_comparators:
+                fi = flashinfer_prefill(case, lengths, 5, 2, flush)
+                if "us" in fi:
+                    fi["ours_speedup"] = round(fi["us"] / (ms * 1e3), 3)
+                pre[name]["flashinfer_sm100"] = fi
+            if (traffic or {}).get(f"prefill_{name}"):
+                t = traffic[f"prefill_{name}"]
+                pre[name]["traffic"] = dict(t, x_algorithmic=round(t["bytes"] / hb, 3))
+            case.pop("gpu_inputs")
+            cases[name] = (case, lengths)
         extra["prefill"] = pre
+        if world == 1 and rank == 0 and not args.no_comparators:
+            extra["decode_comparators"] = {
+                "flashinfer_B64_fp32_state": flashinfer_decode(64, 30, 3, flush, torch.float32),
+                "flashinfer_B64_bf16_state": flashinfer_decode(64, 30, 3, flush, torch.bfloat16)}
         extra["sharded"] = run_sharded(K, rank, world, flush, hbm_peak)
 
     clocks = sampler.stop()
 
     line = None
+    if rank == 0 and world == 1 and not args.quick and not args.no_cpu:
+        # CPU baseline and drift of each prefill case (host only, after the GPU work)
+        for name, (case, lengths) in cases.items():
+            drift, cpu_pre, ro = prefill_drift_and_cpu(case, lengths)
+            extra["prefill"][name]["cpu_baseline"] = cpu_pre
+            extra["prefill"][name]["drift"] = drift
+            fi = extra["prefill"][name].get("flashinfer_sm100", {})
+            if "out" in fi:
+                fo, fs = fi.pop("out"), fi.pop("new_state")
+                fi["out_max_abs_vs_oracle"] = round(float((fo.float() - ro.float()).abs().max()), 6)
+                fi["out_max_abs_vs_ours"] = round(float((fo.float() - case["out"].float()).abs().max()), 6)
+    for v in (extra.get("prefill") or {}).values():
+        fi = v.get("flashinfer_sm100")
+        if fi:
+            fi.pop("out", None)
+            fi.pop("new_state", None)
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
@@ -510,7 +783,7 @@ def run_gpu(args, rank, world, local_rank):
                    "sample": f"decode B={B} qk16_v32, {steps_cpu} steps of the fp32 CPU oracle "
                              f"(torch, {torch.get_num_threads()} threads); "
                              f"{sec * 1e3:.1f} ms/step"}
-        traffic = profile_traffic("decode_B64.md")
+        dec_traffic = (traffic or {}).get("decode")
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -524,7 +797,8 @@ def run_gpu(args, rank, world, local_rank):
                        "parallelism": f"sequence-sharded x{world}, no collective"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                         "traffic": (traffic * 1.0 if traffic else None),
+                         "traffic": (round(dec_traffic["bytes"]) if dec_traffic else None),
+                         "traffic_detail": dec_traffic,
                          "peak_source": f"{peaks_src} hbm_gbs (STREAM-style copy)",
                          "kernel": "gdn_decode_kernel",
                          "algorithmic_bytes_per_launch": step_bytes},
@@ -570,15 +844,22 @@ def run_reference(args):
 
 
 def run_profile(args):
-    """A handful of launches of one case, for ncu captures."""
+    """A handful of launches of one case, for ncu captures.  With --flush-l2 the
+    L2 is evicted before each launch, as between the timed runs."""
     from gdn_kernel_b200 import _lib, kernel as K, workloads as W
 
     torch.cuda.set_device(0)
     _lib.load()
+    flush = L2Flush(torch.cuda.get_device_properties(0).L2_cache_size) if args.flush_l2 else None
+
+    def before():
+        if flush is not None:
+            flush.zero_()
     if args.profile == "decode":
         x = W.make_decode_inputs(args.batch, seed=0, device="cuda")
         out = torch.empty(args.batch, 1, H_V, D, dtype=torch.bfloat16, device="cuda")
         for _ in range(args.launches):
+            before()
             K.gdn_decode(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.scale, out,
                          x.state)
     elif args.profile == "decode_pool":
@@ -587,6 +868,7 @@ def run_profile(args):
                                       device="cuda", state_dtype=sdt)
         out = torch.empty(args.batch, args.seq_len, H_V, D, dtype=torch.bfloat16, device="cuda")
         for _ in range(args.launches):
+            before()
             K.gdn_decode_pool(x.q, x.k, x.v, x.pool, x.indices, x.A_log, x.a, x.dt_bias, x.b,
                               x.scale, out)
     else:
@@ -595,9 +877,12 @@ def run_profile(args):
         x = W.make_prefill_inputs(lengths, seed=0, device="cuda", with_state=args.sequences > 1)
         out = torch.empty(sum(lengths), H_V, D, dtype=torch.bfloat16, device="cuda")
         ns = torch.empty(len(lengths), H_V, D, D, dtype=torch.float32, device="cuda")
+        ws = torch.empty(K.prefill_workspace_bytes(len(lengths), sum(lengths), H_V),
+                         dtype=torch.uint8, device="cuda")
         for _ in range(args.launches):
+            before()
             K.gdn_prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
-                          x.scale, out, ns)
+                          x.scale, out, ns, workspace=ws)
     torch.cuda.synchronize()
     assert _lib.device_status(0) == 0
 
@@ -612,6 +897,11 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=20)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true", help="headline decode + e2e only")
+    ap.add_argument("--no-ncu", action="store_true", help="skip the in-run ncu traffic capture")
+    ap.add_argument("--no-comparators", action="store_true",
+                    help="skip the FlashInfer reference-point timings")
+    ap.add_argument("--flush-l2", action="store_true",
+                    help="--profile: evict L2 (as the timed runs do) before each launch")
     ap.add_argument("--profile", choices=["decode", "decode_pool", "prefill"], default=None)
     ap.add_argument("--seq-len", type=int, default=4, help="--profile decode_pool: tokens per entry")
     ap.add_argument("--pool-dtype", choices=["fp32", "bf16"], default="fp32",
@@ -636,6 +926,16 @@ def main():
             print(json.dumps(run_reference(args)), flush=True)
         return
 
+    traffic = None
+    if world == 1 and not args.quick and not args.no_ncu:
+        # one small ncu capture per kernel group, as child processes, before this
+        # process creates its CUDA context
+        traffic = {
+            "decode": measure_traffic(["decode", "--batch", str(args.batch), "--launches", "3",
+                                       "--flush-l2"], "gdn_decode", 2, 1, "none"),
+            "prefill_T8192": measure_traffic(["prefill", "--tokens", "8192", "--launches", "1",
+                                              "--flush-l2"], "gdn_", 0, 64, "none"),
+        }
     if world > 1:
         import datetime
 
@@ -644,7 +944,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = run_gpu(args, rank, world, local_rank)
+        line = run_gpu(args, rank, world, local_rank, traffic)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

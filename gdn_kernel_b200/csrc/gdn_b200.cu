@@ -701,9 +701,14 @@ extern "C" int gdn_b200_prefill_static(const void* q, const void* k, const void*
                                        int32_t num_qk_heads, int32_t num_v_heads,
                                        int32_t head_dim, void* stream) {
   t_last_error.clear();
+  // The extent checks of the workspace path come first, so that a bad size is
+  // reported as such and not as "too large for the scratch".
   if (int rc = check_heads(num_qk_heads, num_v_heads, head_dim)) return rc;
   if (num_seqs < 0 || total_tokens < 0)
     return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0");
+  if (num_seqs > 65535) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "num_seqs exceeds 65535");
+  if (total_tokens > 0x7fffffffLL - kChunk)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "total_tokens exceeds the int32 TMA coordinate range");
   if (num_seqs == 0) return GDN_B200_OK;
   const uint64_t need = gdn_b200_prefill_workspace_size(num_seqs, total_tokens, num_v_heads);
   if (need > GDN_B200_PREFILL_STATIC_SCRATCH_BYTES)

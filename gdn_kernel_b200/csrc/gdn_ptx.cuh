@@ -19,7 +19,7 @@ enum : unsigned int {
   kStatusOk = 0u,
   kStatusTmaTimeout = 1u,
   kStatusMmaTimeout = 2u,
-  kStatusBadSeqlens = 4u,   // cu_seqlens entry outside [0, total_tokens]
+  kStatusBadSeqlens = 4u,   // cu_seqlens not non-decreasing within [0, total_tokens]
   kStatusSelftestWait = 16u,   // the wait of the bounded-wait self-test ran out
 };
 

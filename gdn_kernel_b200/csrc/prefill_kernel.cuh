@@ -557,9 +557,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   const int row = quad * 32 + lane;   // TMEM lane (matrix row) of this thread
 
   long long s0 = load_cu(p, seq), s1 = load_cu(p, seq + 1);
-  if (s0 < 0 || s1 > p.total_tokens || s0 > p.total_tokens) {
+  if (s0 < 0 || s1 < s0 || s1 > p.total_tokens) {
     if (tid == 0) atomicOr(p.status, kStatusBadSeqlens);   // treated as an empty sequence
-    s1 = s0;
+    s0 = s1 = 0;
   }
   const long long len = s1 - s0;
   const size_t sbase = (static_cast<size_t>(seq) * p.h_v + head) * kHeadDim * kHeadDim;

@@ -99,9 +99,28 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // ---------------------------------------------------------------- chunk table
 constexpr int kTableThreads = 1024;
 
+// Token range [s0, s1) of sequence i, or an empty range (and the bad-seqlens
+// status bit) when the pair is outside 0 <= s0 <= s1 <= total_tokens.
+__device__ __forceinline__ void seq_range(const PrefillParams& p, int i, long long& s0,
+                                          long long& s1) {
+  s0 = load_cu(p, i);
+  s1 = load_cu(p, i + 1);
+  if (s0 < 0 || s1 < s0 || s1 > p.total_tokens) {
+    atomicOr(p.status, kStatusBadSeqlens);   // treated as an empty sequence
+    s0 = s1 = 0;
+  }
+}
+
+// Two passes over the sequences.  Pass 1 scans the per-sequence chunk counts
+// into seq_off.  Valid cu_seqlens (non-decreasing, within [0, total_tokens])
+// describe disjoint sequences, so the total is at most ceil(T / 64) + N =
+// max_chunks, the table's capacity.  Entries that are each in range but not
+// ordered can describe overlapping sequences whose chunks exceed it; then the
+// status bit is set and every sequence is treated as empty, so no kernel ever
+// indexes past max_chunks.  Pass 2 writes the table.
 __global__ void __launch_bounds__(kTableThreads) gdn_chunk_table_kernel(SplitParams sp) {
-  __shared__ int warp_sums[32];
-  __shared__ int carry_s;
+  __shared__ long long warp_sums[32];
+  __shared__ long long carry_s;
   // The prep grid after this one may start its setup now (it waits for this
   // grid's completion before it reads the table).
   pdl_launch_dependents();
@@ -112,56 +131,62 @@ __global__ void __launch_bounds__(kTableThreads) gdn_chunk_table_kernel(SplitPar
   for (int base = 0; base < sp.num_seqs; base += kTableThreads) {
     const int i = base + tid;
     int n = 0;
-    long long s0 = 0, s1 = 0;
     if (i < sp.num_seqs) {
-      s0 = load_cu(p, i);
-      s1 = load_cu(p, i + 1);
-      if (s0 < 0 || s1 > p.total_tokens || s0 > p.total_tokens) {
-        atomicOr(p.status, kStatusBadSeqlens);   // treated as an empty sequence
-        s1 = s0;
-      }
-      n = s1 > s0 ? static_cast<int>((s1 - s0 + kChunk - 1) / kChunk) : 0;
+      long long s0, s1;
+      seq_range(p, i, s0, s1);
+      n = static_cast<int>((s1 - s0 + kChunk - 1) / kChunk);
     }
-    int x = n;   // inclusive warp scan
+    long long x = n;   // inclusive warp scan
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, x, off);
+      const long long y = __shfl_up_sync(0xffffffffu, x, off);
       if (lane >= off) x += y;
     }
     if (lane == 31) warp_sums[warp] = x;
     __syncthreads();
     if (warp == 0) {
-      int w = warp_sums[lane];
+      long long w = warp_sums[lane];
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, w, off);
+        const long long y = __shfl_up_sync(0xffffffffu, w, off);
         if (lane >= off) w += y;
       }
       warp_sums[lane] = w;   // inclusive over warps
     }
     __syncthreads();
-    const int excl = carry_s + (warp > 0 ? warp_sums[warp - 1] : 0) + x - n;
-    if (i < sp.num_seqs) {
-      sp.seq_off[i] = excl;
-      for (int k = 0; k < n; ++k) {
-        ChunkInfo c;
-        c.seq = i;
-        c.cstart = s0 + static_cast<long long>(k) * kChunk;
-        c.clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - c.cstart));
-        sp.table[excl + k] = c;
-      }
-    }
+    const long long excl = carry_s + (warp > 0 ? warp_sums[warp - 1] : 0) + x - n;
+    if (i < sp.num_seqs) sp.seq_off[i] = static_cast<int>(min(excl, static_cast<long long>(sp.max_chunks)));
     __syncthreads();
     if (tid == kTableThreads - 1) carry_s = excl + n;
     __syncthreads();
   }
+  const bool overflow = carry_s > sp.max_chunks;
+  const int total = overflow ? 0 : static_cast<int>(carry_s);
   if (tid == 0) {
-    sp.seq_off[sp.num_seqs] = carry_s;
-    sp.header[0] = carry_s;
+    if (overflow) atomicOr(p.status, kStatusBadSeqlens);
+    sp.seq_off[sp.num_seqs] = total;
+    sp.header[0] = total;
+  }
+  for (int i = tid; i < sp.num_seqs; i += kTableThreads) {
+    if (overflow) {   // overlapping sequences: all are treated as empty
+      sp.seq_off[i] = 0;
+      continue;
+    }
+    long long s0, s1;
+    seq_range(p, i, s0, s1);
+    const int excl = sp.seq_off[i];
+    const int n = static_cast<int>((s1 - s0 + kChunk - 1) / kChunk);
+    for (int k = 0; k < n; ++k) {
+      ChunkInfo c;
+      c.seq = i;
+      c.cstart = s0 + static_cast<long long>(k) * kChunk;
+      c.clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - c.cstart));
+      sp.table[excl + k] = c;
+    }
   }
   // Table slots past the last chunk get clen = 0: the prep kernel's CTAs for
   // them read one entry and exit.
-  for (int i = carry_s + tid; i < sp.max_chunks; i += kTableThreads) {
+  for (int i = total + tid; i < sp.max_chunks; i += kTableThreads) {
     ChunkInfo c;
     c.seq = -1;
     c.clen = 0;

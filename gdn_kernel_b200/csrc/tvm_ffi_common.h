@@ -9,6 +9,8 @@
 #include <tvm/ffi/extra/c_env_api.h>
 #include <tvm/ffi/function.h>
 
+#include <cuda_runtime.h>
+
 #include <cstdint>
 #include <string>
 #include <vector>
@@ -48,6 +50,31 @@ inline void check_rc(int rc) {
   if (rc == GDN_B200_ERR_INVALID_ARGUMENT) TVM_FFI_THROW(ValueError) << gdn_b200_last_error();
   if (rc != GDN_B200_OK) TVM_FFI_THROW(RuntimeError) << gdn_b200_last_error();
 }
+
+// Makes the tensors' device current for the whole call (the C ABI launches on,
+// and looks up per-device state for, the current device) and restores the
+// caller's device on exit.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(const DLDevice& dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess)
+      TVM_FFI_THROW(RuntimeError) << "cudaGetDevice failed";
+    if (prev_ != dev.device_id) {
+      cudaError_t e = cudaSetDevice(dev.device_id);
+      if (e != cudaSuccess) TVM_FFI_THROW(RuntimeError) << "cudaSetDevice: " << cudaGetErrorString(e);
+      switched_ = true;
+    }
+  }
+  ~DeviceGuard() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+ private:
+  int prev_ = 0;
+  bool switched_ = false;
+};
 
 inline void* env_stream(const DLDevice& dev) {
   return TVMFFIEnvGetStream(dev.device_type, dev.device_id);

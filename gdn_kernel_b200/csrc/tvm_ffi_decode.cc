@@ -24,6 +24,7 @@ void GdnDecode(TensorView q, TensorView k, TensorView v, TensorView state, Tenso
   check_tensor(output, "output", kDLBfloat, 16, {B, 1, H_v, D}, dev);
   check_tensor(new_state, "new_state", kDLFloat, 32, {B, H_v, D, D}, dev);
   const float* st = optional_state(state, "state", {B, H_v, D, D}, dev);
+  DeviceGuard guard(dev);
   check_rc(gdn_b200_decode(ptr(q), ptr(k), ptr(v), st, static_cast<const float*>(ptr(A_log)),
                            ptr(a), static_cast<const float*>(ptr(dt_bias)), ptr(b), scale,
                            ptr(output), static_cast<float*>(ptr(new_state)), B,

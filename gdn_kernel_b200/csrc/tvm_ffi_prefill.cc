@@ -34,15 +34,12 @@ void GdnPrefill(TensorView q, TensorView k, TensorView v, TensorView state, Tens
   // The reference signature carries no workspace: take the two-stage path's
   // workspace from the stream-ordered pool of this device and give it back on
   // the same stream, so the call stays asynchronous.
+  DeviceGuard guard(dev);
   cudaStream_t stream = static_cast<cudaStream_t>(env_stream(dev));
   const uint64_t ws_bytes = gdn_b200_prefill_workspace_size(N, T, static_cast<int32_t>(H_v));
   void* ws = nullptr;
   if (ws_bytes > 0) {
-    int prev = 0;
-    cudaGetDevice(&prev);
-    if (prev != dev.device_id) cudaSetDevice(dev.device_id);
     cudaError_t e = cudaMallocAsync(&ws, ws_bytes, stream);
-    if (prev != dev.device_id) cudaSetDevice(prev);
     if (e != cudaSuccess) TVM_FFI_THROW(RuntimeError) << "workspace: " << cudaGetErrorString(e);
   }
   const int rc = gdn_b200_prefill_ws(ptr(q), ptr(k), ptr(v), st,

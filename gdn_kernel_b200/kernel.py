@@ -58,6 +58,14 @@ def _stream(device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _launch(dev, fn, *args) -> None:
+    """Call a C entry point with ``dev`` current (the library launches on, and
+    sets up, the current device) and ``dev``'s current torch stream as the last
+    argument; raise on an error code."""
+    with torch.cuda.device(dev):
+        _lib.check(fn(*args, _stream(dev)))
+
+
 def _cuda_device(q: torch.Tensor):
     _require(isinstance(q, torch.Tensor) and q.is_cuda, "q must be a CUDA tensor")
     return q.device
@@ -87,9 +95,9 @@ def gdn_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state) -
     if state is not None:
         _check(state, "state", torch.float32, (B, h_v, D, D), dev)
     lib = _lib.load()
-    _lib.check(lib.gdn_b200_decode(
+    _launch(dev, lib.gdn_b200_decode,
         _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
-        float(scale or 0.0), _ptr(output), _ptr(new_state), B, h_qk, h_v, D, _stream(dev)))
+        float(scale or 0.0), _ptr(output), _ptr(new_state), B, h_qk, h_v, D)
 
 
 def gdn_decode_pool(q, k, v, state_pool, state_indices, A_log, a, dt_bias, b, scale, output,
@@ -143,12 +151,12 @@ def gdn_decode_pool(q, k, v, state_pool, state_indices, A_log, a, dt_bias, b, sc
     if intermediate_states is not None:
         _check(intermediate_states, "intermediate_states", sdt, (P, T, h_v, D, D), dev)
     lib = _lib.load()
-    _lib.check(lib.gdn_b200_decode_pool(
+    _launch(dev, lib.gdn_b200_decode_pool,
         _ptr(q), _ptr(k), _ptr(v), _ptr(state_pool), _ptr(new_state_pool),
         1 if sdt == torch.bfloat16 else 0, _ptr(state_indices), _ptr(output_state_indices),
         1 if state_indices.dtype == torch.int64 else 0, _ptr(intermediate_states),
         _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b), float(scale or 0.0), _ptr(output),
-        B, T, P, h_qk, h_v, D, _stream(dev)))
+        B, T, P, h_qk, h_v, D)
 
 
 def gdn_mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
@@ -194,8 +202,8 @@ def state_affine(state, transfer, offset, out=None):
     if out is None:
         out = torch.empty_like(offset)
     _check(out, "out", torch.float32, (H, HEAD_DIM, HEAD_DIM), dev)
-    _lib.check(_lib.load().gdn_b200_state_affine(_ptr(state), _ptr(transfer), _ptr(offset),
-                                                 _ptr(out), H, _stream(dev)))
+    _launch(dev, _lib.load().gdn_b200_state_affine, _ptr(state), _ptr(transfer), _ptr(offset),
+                                                 _ptr(out), H)
     return out
 
 
@@ -248,7 +256,7 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
             _ptr(cu_seqlens), 1 if cu_seqlens.dtype == torch.int64 else 0, float(scale or 0.0),
             _ptr(output), _ptr(new_state), N, T, h_qk, h_v, D)
     if path == "fused" or N == 0:
-        _lib.check(lib.gdn_b200_prefill(*args, _stream(dev)))
+        _launch(dev, lib.gdn_b200_prefill, *args)
         return
     need = prefill_workspace_bytes(N, T, h_v)
     if workspace is None:
@@ -256,9 +264,8 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
     _require(isinstance(workspace, torch.Tensor) and workspace.device == dev
              and workspace.numel() * workspace.element_size() >= need,
              f"workspace must be a tensor on {dev} of at least {need} bytes")
-    _lib.check(lib.gdn_b200_prefill_ws(*args, _ptr(workspace),
-                                       workspace.numel() * workspace.element_size(),
-                                       _stream(dev)))
+    _launch(dev, lib.gdn_b200_prefill_ws, *args, _ptr(workspace),
+                                       workspace.numel() * workspace.element_size())
 
 
 def gdn_prefill_prepare(q, k, A_log, a, dt_bias, b, cu_seqlens, workspace) -> None:
@@ -277,10 +284,10 @@ def gdn_prefill_prepare(q, k, A_log, a, dt_bias, b, cu_seqlens, workspace) -> No
     _check(a, "a", torch.bfloat16, (T, h_v), dev)
     _check(dt_bias, "dt_bias", torch.float32, (h_v,), dev)
     _check(b, "b", torch.bfloat16, (T, h_v), dev)
-    _lib.check(_lib.load().gdn_b200_prefill_prepare(
+    _launch(dev, _lib.load().gdn_b200_prefill_prepare,
         _ptr(q), _ptr(k), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b), _ptr(cu_seqlens),
         1 if cu_seqlens.dtype == torch.int64 else 0, N, T, h_qk, h_v, D, _ptr(workspace),
-        workspace.numel() * workspace.element_size(), _stream(dev)))
+        workspace.numel() * workspace.element_size())
 
 
 def gdn_prefill_recur(k, v, state, scale, output, new_state, num_seqs, num_v_heads,
@@ -299,10 +306,10 @@ def gdn_prefill_recur(k, v, state, scale, output, new_state, num_seqs, num_v_hea
     _check(new_state, "new_state", torch.float32, (num_seqs, num_v_heads, D, D), dev)
     if state is not None:
         _check(state, "state", torch.float32, (num_seqs, num_v_heads, D, D), dev)
-    _lib.check(_lib.load().gdn_b200_prefill_recur(
+    _launch(dev, _lib.load().gdn_b200_prefill_recur,
         _ptr(k), _ptr(v), _ptr(state), float(scale or 0.0), _ptr(output), _ptr(new_state),
         num_seqs, T, h_qk, num_v_heads, D, _ptr(workspace),
-        workspace.numel() * workspace.element_size(), _stream(dev)))
+        workspace.numel() * workspace.element_size())
 
 
 def decode(q, k, v, state, A_log, a, dt_bias, b, scale: float = 0.0, *, in_place: bool = False):

@@ -40,7 +40,7 @@ extern "C" {
 /* Device status bits (read with gdn_b200_device_status). */
 #define GDN_B200_STATUS_TMA_TIMEOUT 1u   /* a prefill TMA wait exceeded its bound */
 #define GDN_B200_STATUS_MMA_TIMEOUT 2u   /* a prefill tensor-core wait exceeded its bound */
-#define GDN_B200_STATUS_BAD_SEQLENS 4u   /* a cu_seqlens entry was outside [0, total_tokens] */
+#define GDN_B200_STATUS_BAD_SEQLENS 4u   /* cu_seqlens not non-decreasing within [0, total_tokens] */
 #define GDN_B200_STATUS_BAD_INDEX 8u     /* a state-pool index was >= pool_size */
 #define GDN_B200_STATUS_SELFTEST_WAIT 16u /* gdn_b200_selftest_wait_timeout's wait ran out */
 

@@ -6,10 +6,12 @@
 # layout (ref solution/cuda/kernel.cu:10-11, kernel_prefill.cu:11-12) to pin
 # the CPU oracle against the reference's real arithmetic.
 #
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+#   REFERENCE_ROOT defaults to $GDN_REFERENCE_ROOT, else a `reference` directory
+#   beside this repository.
 set -euo pipefail
-REF="${1:-/root/reference}"
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+REF="${1:-${GDN_REFERENCE_ROOT:-$(dirname "$(dirname "$HERE")")/reference}}"
 OUT="$HERE/_ref"
 if [ ! -f "$REF/solution/cuda/kernel.cu" ]; then
   echo "reference sources not found under $REF; nothing to build" >&2

@@ -220,3 +220,39 @@ def test_wide_chain_matches_per_sequence_calls():
     assert _lib.device_status(torch.cuda.current_device()) == 0
     ro, rs = _oracle(x)
     assert_prefill_close(out.cpu(), ns.cpu(), ro, rs)
+
+
+def test_unordered_cu_seqlens_flagged_and_bounded():
+    """cu_seqlens whose entries are each in range but not ordered ([0, T, 0, T])
+    describe overlapping sequences with more chunks than the table holds.  The
+    split path sets the bad-seqlens status bit, treats every sequence as empty
+    (each final state is its initial state) and writes nothing past its
+    workspace; a descending pair alone is flagged too."""
+    T = 1000
+    x = W.make_prefill_inputs([T], seed=41, device="cuda")
+    cu = torch.tensor([0, T, 0, T], dtype=torch.int32, device="cuda")
+    state = torch.randn(3, 32, 128, 128, device="cuda") * 0.02
+    need = K.prefill_workspace_bytes(3, T, 32)
+    guard = 1 << 20
+    buf = torch.full((need + guard,), 0x5A, dtype=torch.uint8, device="cuda")
+    out = torch.zeros(T, 32, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty_like(state)
+    K.gdn_prefill(x.q, x.k, x.v, state, x.A_log, x.a, x.dt_bias, x.b, cu, x.scale, out, ns,
+                  workspace=buf[:need])
+    torch.cuda.synchronize()
+    status = _lib.device_status(torch.cuda.current_device())
+    assert status & _lib.STATUS_BAD_SEQLENS
+    assert status & ~_lib.STATUS_BAD_SEQLENS == 0
+    assert torch.all(buf[need:] == 0x5A)
+    assert torch.equal(ns, state)
+    assert torch.count_nonzero(out) == 0
+    # a descending pair within the table's capacity: flagged, the others still run
+    cu2 = torch.tensor([0, 50, 20, 100], dtype=torch.int64, device="cuda")
+    out2 = torch.empty(100, 32, 128, dtype=torch.bfloat16, device="cuda")
+    x2 = W.make_prefill_inputs([100], seed=42, device="cuda")
+    ns2 = torch.empty(3, 32, 128, 128, device="cuda")
+    K.gdn_prefill(x2.q, x2.k, x2.v, None, x2.A_log, x2.a, x2.dt_bias, x2.b, cu2, x2.scale, out2,
+                  ns2)
+    torch.cuda.synchronize()
+    assert _lib.device_status(torch.cuda.current_device()) == _lib.STATUS_BAD_SEQLENS
+    assert torch.count_nonzero(ns2[1]) == 0

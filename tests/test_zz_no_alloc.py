@@ -42,9 +42,12 @@ def _call_static(x, out, ns):
 
 
 def test_static_scratch_prefill_matches_workspace_entry_point():
-    # Two calls in a row with different inputs: the second call runs on the
-    # scratch contents the first one left behind.
-    for lengths, seed in (([150, 0, 64, 33], 71), ([700, 1, 129], 72)):
+    # Calls in a row with different inputs: each later call runs on the scratch
+    # contents the call before it left behind.  Both entry points launch the
+    # same kernels on the same tiles, so the results agree bit for bit.  The
+    # 1100-token single sequence takes the one-sequence path that runs in
+    # overlapping pieces (at least 16 chunks).
+    for lengths, seed in (([150, 0, 64, 33], 71), ([700, 1, 129], 72), ([1100], 73)):
         x = W.make_prefill_inputs(lengths, seed=seed, device="cuda")
         T = sum(lengths)
         assert K.prefill_workspace_bytes(len(lengths), T, 32) <= STATIC_SCRATCH_BYTES
@@ -56,6 +59,8 @@ def test_static_scratch_prefill_matches_workspace_entry_point():
                            x.scale, path="split")
         torch.cuda.synchronize()
         assert _lib.device_status(torch.cuda.current_device()) == 0
+        assert torch.equal(out, ro), lengths
+        assert torch.equal(ns, rs), lengths
         assert_prefill_close(out.cpu(), ns.cpu(), ro.cpu(), rs.cpu(), lengths)
 
 
@@ -67,3 +72,8 @@ def test_static_scratch_refuses_oversized_problem():
                                      128, z)
     assert rc == _lib.GDN_B200_ERR_INVALID_ARGUMENT
     assert b"static prefill scratch" in lib.gdn_b200_last_error()
+    # a bad extent is reported as such, before the size comparison
+    rc = lib.gdn_b200_prefill_static(z, z, z, z, z, z, z, z, z, 0, 0.0, z, z, 70000, 100, 16, 32,
+                                     128, z)
+    assert rc == _lib.GDN_B200_ERR_INVALID_ARGUMENT
+    assert b"num_seqs" in lib.gdn_b200_last_error()
