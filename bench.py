@@ -70,46 +70,50 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-NCU_METRICS = "dram__bytes_read.sum,dram__bytes_write.sum,lts__t_sectors_op_write.sum"
+NCU_METRICS = "dram__bytes_read.sum,dram__bytes_write.sum"
+TRAFFIC_RANGE = "gdn_traffic"
 
 
 def _ncu_rows(csv_path):
-    """(kernel name, metric name, value) rows of an ncu --csv log."""
+    """(ID, kernel name, metric name, value) rows of an ncu --csv log."""
     import csv
-    rows = []
     with open(csv_path, newline="") as f:
         lines = [ln for ln in f if ln.startswith('"')]
+    rows = []
     for rec in csv.DictReader(lines):
         try:
             val = float(str(rec.get("Metric Value", "")).replace(",", ""))
         except ValueError:
             continue
-        rows.append((rec.get("Kernel Name", ""), rec.get("Metric Name", ""),
-                     val * {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(
-                         rec.get("Metric Unit", "byte"), 1.0), rec.get("ID", "")))
+        rows.append((int(rec.get("ID", "0") or 0), rec.get("Kernel Name", ""),
+                     rec.get("Metric Name", ""), val))
     return rows
 
 
-def measure_traffic(profile_args, kernel_regex, skip, count, cache_control, timeout_s=600):
-    """DRAM traffic of the kernels of one small invocation, from one ncu capture
-    of this file's --profile mode (run as a child process before this process
-    touches the GPU).  Writes are counted where they enter L2
-    (lts__t_sectors_op_write x 32 B): a kernel's dirty lines reach DRAM after its
-    window closes (when the next kernel evicts them), so dram__bytes_write.sum
-    alone undercounts them.  Reads are dram__bytes_read.sum.  Returns per-launch
-    totals summed over the captured kernels, or None when ncu is unavailable."""
+def measure_traffic(profile_args, timeout_s=600):
+    """DRAM traffic of one launch of this file's --profile case, from one ncu
+    capture (a child process started before this process touches the GPU).
+
+    The profile run brackets its last launch and one evict-only kernel after it
+    (a read of 2x the L2 size of clean data) in the NVTX range TRAFFIC_RANGE,
+    and ncu captures exactly the kernels inside it (--cache-control none: no
+    flush by ncu; the profile case itself evicts L2 before the launch).  A
+    kernel's dirty lines reach DRAM after its window closes, when the next
+    kernel evicts them, so the launch's traffic is its kernels' DRAM reads and
+    writes plus the evict kernel's DRAM writes (that kernel writes nothing else
+    of its own).  Returns None when ncu is unavailable or the capture fails."""
     import shutil
     import tempfile
     ncu = shutil.which("ncu")
     if ncu is None:
         return None
+    base = ["--metrics", NCU_METRICS, "--clock-control", "none", "--cache-control", "none",
+            "--nvtx", "--nvtx-include", f"{TRAFFIC_RANGE}/"]
     with tempfile.TemporaryDirectory() as td:
         log_path = os.path.join(td, "traffic.csv")
-        cmd = [ncu, "--metrics", NCU_METRICS, "--clock-control", "none",
-               "--cache-control", cache_control, "-k", f"regex:{kernel_regex}", "-s", str(skip),
-               "-c", str(count), "--csv", "--print-units", "base", "--log-file", log_path,
-               sys.executable,
-               os.path.abspath(__file__), "--profile", *profile_args]
+        cmd = [ncu, *base, "--csv", "--print-units", "base", "--log-file", log_path,
+               sys.executable, os.path.abspath(__file__), "--profile", *profile_args,
+               "--flush-l2", "--traffic-range"]
         try:
             res = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
                                  timeout=timeout_s)
@@ -120,26 +124,26 @@ def measure_traffic(profile_args, kernel_regex, skip, count, cache_control, time
             log(f"traffic capture failed (rc={res.returncode}): {res.stdout[-2000:]}")
             return None
         rows = _ncu_rows(log_path)
-    if not rows:
+    per = {}
+    for kid, kname, metric, val in rows:
+        d = per.setdefault(kid, {"name": kname})
+        d[metric] = val
+    if not per:
         return None
-    tot = {"dram_read": 0.0, "dram_write_in_window": 0.0, "l2_write": 0.0}
-    kernels = {}
-    for kname, metric, val, kid in rows:
-        key = {"dram__bytes_read.sum": "dram_read", "dram__bytes_write.sum": "dram_write_in_window",
-               "lts__t_sectors_op_write.sum": "l2_write"}.get(metric)
-        if key is None:
-            continue
-        if key == "l2_write":
-            val *= 32.0
-        tot[key] += val
-        kernels.setdefault(kname.split("(")[0].split("<")[0], set()).add(kid)
-    tot["bytes"] = tot["dram_read"] + max(tot["l2_write"], tot["dram_write_in_window"])
-    tot["launches"] = {k: len(v) for k, v in kernels.items()}
-    tot["command"] = " ".join(["ncu", "--metrics", NCU_METRICS, "--clock-control", "none",
-                               "--cache-control", cache_control, "-k", f"regex:{kernel_regex}",
-                               "-s", str(skip), "-c", str(count), "python bench.py --profile",
-                               *profile_args])
-    return tot
+    ids = sorted(per)
+    *own, evict = ids   # the evict-only kernel closes the range
+    out = {"dram_read": sum(per[i].get("dram__bytes_read.sum", 0.0) for i in own),
+           "dram_write_in_window": sum(per[i].get("dram__bytes_write.sum", 0.0) for i in own),
+           "dram_write_drained_after": per[evict].get("dram__bytes_write.sum", 0.0)}
+    out["bytes"] = out["dram_read"] + out["dram_write_in_window"] + out["dram_write_drained_after"]
+    names = {}
+    for i in own:
+        n = per[i]["name"].split("(")[0].replace("void ", "").split("<")[0].strip()
+        names[n] = names.get(n, 0) + 1
+    out["kernels"] = names
+    out["command"] = " ".join(["ncu", *base, "python bench.py --profile", *profile_args,
+                               "--flush-l2", "--traffic-range"])
+    return out
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -219,6 +223,15 @@ class L2Flush:
 
     def zero_(self):
         self.w.zero_()
+        torch.sum(self.r, dim=0, out=self.sink)
+        # keep the GPU busy a little longer, so that the host has enqueued the
+        # timed launch before the GPU reaches the start event (host-side
+        # argument checks then never show up as device time)
+        torch.cuda._sleep(100_000)
+
+    def evict_clean(self):
+        """Read 2x the L2 size of clean data: evicts (writes back) every dirty
+        line and writes nothing itself."""
         torch.sum(self.r, dim=0, out=self.sink)
 
 
@@ -855,22 +868,31 @@ def run_profile(args):
     def before():
         if flush is not None:
             flush.zero_()
+        if args.traffic_range and i == args.launches - 1:
+            torch.cuda.nvtx.range_push(TRAFFIC_RANGE)
+
+    def after():
+        if args.traffic_range and i == args.launches - 1:
+            flush.evict_clean()
+            torch.cuda.nvtx.range_pop()
     if args.profile == "decode":
         x = W.make_decode_inputs(args.batch, seed=0, device="cuda")
         out = torch.empty(args.batch, 1, H_V, D, dtype=torch.bfloat16, device="cuda")
-        for _ in range(args.launches):
+        for i in range(args.launches):
             before()
             K.gdn_decode(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.scale, out,
                          x.state)
+            after()
     elif args.profile == "decode_pool":
         sdt = torch.bfloat16 if args.pool_dtype == "bf16" else torch.float32
         x = W.make_pool_decode_inputs(args.batch, args.seq_len, 2 * args.batch, seed=7000,
                                       device="cuda", state_dtype=sdt)
         out = torch.empty(args.batch, args.seq_len, H_V, D, dtype=torch.bfloat16, device="cuda")
-        for _ in range(args.launches):
+        for i in range(args.launches):
             before()
             K.gdn_decode_pool(x.q, x.k, x.v, x.pool, x.indices, x.A_log, x.a, x.dt_bias, x.b,
                               x.scale, out)
+            after()
     else:
         lengths = ([args.tokens] if args.sequences == 1
                    else W.varlen_lengths(args.sequences, 128, args.tokens, seed=3))
@@ -879,10 +901,11 @@ def run_profile(args):
         ns = torch.empty(len(lengths), H_V, D, D, dtype=torch.float32, device="cuda")
         ws = torch.empty(K.prefill_workspace_bytes(len(lengths), sum(lengths), H_V),
                          dtype=torch.uint8, device="cuda")
-        for _ in range(args.launches):
+        for i in range(args.launches):
             before()
             K.gdn_prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
                           x.scale, out, ns, workspace=ws)
+            after()
     torch.cuda.synchronize()
     assert _lib.device_status(0) == 0
 
@@ -902,6 +925,9 @@ def main():
                     help="skip the FlashInfer reference-point timings")
     ap.add_argument("--flush-l2", action="store_true",
                     help="--profile: evict L2 (as the timed runs do) before each launch")
+    ap.add_argument("--traffic-range", action="store_true",
+                    help="--profile with --flush-l2: bracket the last launch and an evict-only "
+                         "kernel in an NVTX range (the in-run traffic capture)")
     ap.add_argument("--profile", choices=["decode", "decode_pool", "prefill"], default=None)
     ap.add_argument("--seq-len", type=int, default=4, help="--profile decode_pool: tokens per entry")
     ap.add_argument("--pool-dtype", choices=["fp32", "bf16"], default="fp32",
@@ -931,10 +957,8 @@ def main():
         # one small ncu capture per kernel group, as child processes, before this
         # process creates its CUDA context
         traffic = {
-            "decode": measure_traffic(["decode", "--batch", str(args.batch), "--launches", "3",
-                                       "--flush-l2"], "gdn_decode", 2, 1, "none"),
-            "prefill_T8192": measure_traffic(["prefill", "--tokens", "8192", "--launches", "1",
-                                              "--flush-l2"], "gdn_", 0, 64, "none"),
+            "decode": measure_traffic(["decode", "--batch", str(args.batch), "--launches", "3"]),
+            "prefill_T8192": measure_traffic(["prefill", "--tokens", "8192", "--launches", "2"]),
         }
     if world > 1:
         import datetime
