@@ -40,6 +40,10 @@ _SIGNATURES = {
     "gdn_b200_prefill": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int32,
                                         ctypes.c_double, _P, _P, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P]),
+    "gdn_b200_prefill_fused": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int32,
+                                              ctypes.c_double, _P, _P, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, _P]),
     "gdn_b200_prefill_workspace_size": (ctypes.c_uint64, [ctypes.c_int64, ctypes.c_int64,
                                                          ctypes.c_int32]),
     "gdn_b200_prefill_ws": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int32,

@@ -71,14 +71,16 @@ int device_setup(unsigned int** status_out) {
     e = cudaFuncSetAttribute(gdn_prefill_prep_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kP1Smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prep smem)");
-    e = cudaFuncSetAttribute(gdn_prefill_chain_kernel<64>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(ChainLayout<64>::kSmem));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem)");
-    e = cudaFuncSetAttribute(gdn_prefill_chain_kernel<128>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(ChainLayout<128>::kSmem));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem, wide)");
+    for (auto fn : {gdn_prefill_chain_kernel<64, false>, gdn_prefill_chain_kernel<64, true>}) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(ChainLayout<64>::kSmem));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem)");
+    }
+    for (auto fn : {gdn_prefill_chain_kernel<128, false>, gdn_prefill_chain_kernel<128, true>}) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(ChainLayout<128>::kSmem));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem, wide)");
+    }
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
@@ -360,6 +362,12 @@ SplitParams split_params(const PrefillParams& p, void* workspace, const SplitLay
   sp.records = ws + L.off_rec;
   sp.num_seqs = static_cast<int>(num_seqs);
   sp.max_chunks = static_cast<int>(L.max_chunks);
+  sp.ring_rows = static_cast<int>(L.max_chunks);
+  sp.group = 1;
+  sp.block = 1;
+  sp.window = 0;
+  sp.scan = 0;
+  sp.win_seq = reinterpret_cast<int*>(ws + L.off_win);
   sp.c_lo = 0;
   sp.c_hi = std::numeric_limits<int>::max();
   sp.wait_table = 0;
@@ -426,13 +434,20 @@ void launch_prepare(const SplitParams& sp, const CUtensorMap& tq, const CUtensor
 // ceil(n / SMs) waves of 1.2 t, so the wide form wins once 2n > SMs.  (The
 // one-sequence pieces path keeps the narrow form: its idle SMs run the prep.)
 void launch_recur(const SplitParams& sp, const CUtensorMap& tk, const CUtensorMap& tv,
-                  int64_t num_seqs, int32_t num_v_heads, cudaStream_t st) {
-  if (2 * num_seqs * num_v_heads > static_cast<int64_t>(device_sm_count())) {
-    const dim3 g(static_cast<unsigned>(num_v_heads), static_cast<unsigned>(num_seqs));
-    gdn_prefill_chain_kernel<128><<<g, kC2Threads, ChainLayout<128>::kSmem, st>>>(tk, tv, sp);
+                  int64_t num_seqs, int32_t num_v_heads, cudaStream_t st, bool allow_wide = true) {
+  // (num_seqs: CTA rows of the grid; with sp.scan each row runs a window's candidates)
+  const bool wide = allow_wide && 2 * num_seqs * num_v_heads > static_cast<int64_t>(device_sm_count());
+  const dim3 g(static_cast<unsigned>((wide ? 1 : 2) * num_v_heads), static_cast<unsigned>(num_seqs));
+  if (wide) {
+    if (sp.scan)
+      gdn_prefill_chain_kernel<128, true><<<g, kC2Threads, ChainLayout<128>::kSmem, st>>>(tk, tv, sp);
+    else
+      gdn_prefill_chain_kernel<128, false><<<g, kC2Threads, ChainLayout<128>::kSmem, st>>>(tk, tv, sp);
   } else {
-    const dim3 g(static_cast<unsigned>(2 * num_v_heads), static_cast<unsigned>(num_seqs));
-    gdn_prefill_chain_kernel<64><<<g, kC2Threads, ChainLayout<64>::kSmem, st>>>(tk, tv, sp);
+    if (sp.scan)
+      gdn_prefill_chain_kernel<64, true><<<g, kC2Threads, ChainLayout<64>::kSmem, st>>>(tk, tv, sp);
+    else
+      gdn_prefill_chain_kernel<64, false><<<g, kC2Threads, ChainLayout<64>::kSmem, st>>>(tk, tv, sp);
   }
 }
 
@@ -481,9 +496,8 @@ void launch_two_stage(const SplitParams& sp, const CUtensorMap& tq, const CUtens
     const int hi = i + 1 == count ? std::numeric_limits<int>::max()
                                   : std::max(lo + 1, static_cast<int>(std::lround(nch * end)));
     SplitParams piece = sp;
-    piece.c_lo = lo;
+    piece.c_lo = lo;   // a later piece continues from new_state (the chain kernel's rule)
     piece.c_hi = hi;
-    if (i > 0) piece.base.state = sp.base.new_state;   // where the previous piece ended
     const long long items = (std::min<long long>(hi, nch) - lo) * num_v_heads;
     if (i == 0)
       launch_table_then_prep(piece, tq, tk, items, 2LL * sms, st);
@@ -494,10 +508,151 @@ void launch_two_stage(const SplitParams& sp, const CUtensorMap& tq, const CUtens
   }
 }
 
+// A two-stage call whose records do not all fit the record rows of the
+// workspace (a ring of sp.ring_rows rows): consecutive windows of W =
+// ring_rows / 2 table chunks, the records of chunk g in row g % ring_rows, so
+// that a window's records fill one half of the ring while the chain of the
+// window before it reads the other half.  The host knows only an upper bound
+// of the chunk count (ceil(T / 64) + N); windows past the table's real end
+// find no items and no chunks.
+//  * One sequence: as in the one-sequence pieces, the prep of window i + 1 is
+//    launched to overlap the chain of window i on the SMs that chain (64-column
+//    CTAs) leaves free, and completes only after it; the prep of window i + 2
+//    starts after the chain of window i + 1 has started, i.e. after the chain
+//    of window i (the last reader of its half) has completed.
+//  * Several sequences: the table interleaves groups of K sequences (K H_v
+//    chain CTAs fill the SMs once) in rounds of W / K chunks per member, so
+//    each window holds about W / K consecutive chunks of each of K sequences
+//    and its chain runs them all at once; the chain then fills the GPU, so
+//    each window's prep runs on all SMs after the previous chain.  A window's
+//    records (W H_v records) are read back while still in L2.
+void launch_windows(const SplitParams& sp0, const CUtensorMap& tq, const CUtensorMap& tk,
+                    const CUtensorMap& tv, const SplitLayout& L, int64_t num_seqs,
+                    int32_t num_v_heads, cudaStream_t st) {
+  const int sms = device_sm_count();
+  SplitParams sp = sp0;
+  const long long window = sp.ring_rows / 2;
+  const bool interleave = num_seqs > 1;
+  if (interleave) {
+    sp.group = std::max(1, std::min<int>(kMaxGroup, sms / std::max(1, num_v_heads)));
+    sp.block = static_cast<int>(std::max<long long>(1, window / sp.group));
+    sp.window = static_cast<int>(window);
+  }
+  const long long free_ctas = 2LL * std::max(1, sms - 2 * num_v_heads);
+  for (long long lo = 0, i = 0; lo < L.max_chunks; lo += window, ++i) {
+    SplitParams win = sp;
+    win.c_lo = static_cast<int>(lo);
+    win.c_hi = static_cast<int>(std::min<long long>(lo + window, L.max_chunks));
+    const long long items = (win.c_hi - win.c_lo) * static_cast<long long>(num_v_heads);
+    if (i == 0)
+      launch_table_then_prep(win, tq, tk, items, 2LL * sms, st);
+    else if (interleave)
+      launch_prep(win, tq, tk, items, 2LL * sms, false, st);
+    else
+      launch_prep(win, tq, tk, items, free_ctas, true, st);
+    if (!interleave) {
+      launch_recur(win, tk, tv, num_seqs, num_v_heads, st, false);
+    } else if (i == 0) {
+      // every sequence gets a CTA row once (empty sequences copy their state)
+      launch_recur(win, tk, tv, num_seqs, num_v_heads, st, true);
+    } else {
+      win.scan = 1;   // K CTA rows run the window's candidate sequences
+      launch_recur(win, tk, tv, sp.group, num_v_heads, st, true);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- record ring
+// The reference's prefill `kernel` takes no workspace and allocates nothing
+// (ref solution/cuda/kernel_prefill.cu:300-337).  gdn_b200_prefill keeps that
+// contract at the speed of the two-stage path: its workspace is a record ring
+// that is part of this library's device image (GDN_B200_PREFILL_RING_BYTES on
+// every GPU that loads the library, held until the process exits).  The chunk
+// tables take its front; the rest holds rows of H_v records.  A problem whose
+// records all fit runs exactly as with a caller workspace; a larger one runs
+// in windows (launch_windows).  Calls on different streams hand the ring over
+// through an event: each call's stream waits for the previous call's last
+// kernel, and the host never blocks.  (A stream under graph capture skips
+// that handoff; captured calls must not overlap other calls on the device.)
+static __device__ __align__(1024) uint8_t g_prefill_ring[GDN_B200_PREFILL_RING_BYTES];
+
+struct RingState {
+  void* ptr = nullptr;          // device address of g_prefill_ring on this device
+  cudaEvent_t done = nullptr;   // recorded after the last call's final kernel
+  bool recorded = false;
+};
+RingState g_ring[kMaxDevices];
+std::mutex g_ring_mu;
+
 }  // namespace
 }  // namespace gdn
 
 extern "C" int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* state,
+                                const float* A_log, const void* a, const float* dt_bias,
+                                const void* b, const void* cu_seqlens,
+                                int32_t cu_seqlens_is_int64, double scale, void* output,
+                                float* new_state, int64_t num_seqs, int64_t total_tokens,
+                                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                                void* stream) {
+  t_last_error.clear();
+  PrefillParams p;
+  CUtensorMap tq, tk, tv;
+  if (int rc = prefill_setup(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64,
+                             scale, output, new_state, num_seqs, total_tokens, num_qk_heads,
+                             num_v_heads, head_dim, &p, &tq, &tk, &tv))
+    return rc;
+  if (num_seqs == 0) return GDN_B200_OK;
+  // Ring geometry: the tables first, then as many record rows as fit.
+  const SplitLayout front = split_layout(num_seqs, total_tokens, num_v_heads, 0, true);
+  const uint64_t row_bytes = static_cast<uint64_t>(num_v_heads) * kRecBytes;
+  const uint64_t ring = GDN_B200_PREFILL_RING_BYTES;
+  const long long rows =
+      front.off_rec < ring ? static_cast<long long>((ring - front.off_rec) / row_bytes) : 0;
+  if (rows < 2)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT,
+                "problem too large for the prefill record ring (its chunk tables or two rows "
+                "of records do not fit); use gdn_b200_prefill_ws with a caller workspace");
+  if (front.max_chunks > 0x7fffffffLL) return fail(GDN_B200_ERR_INVALID_ARGUMENT, "too many chunks");
+  const long long use_rows = std::min<long long>(rows, front.max_chunks);
+  const SplitLayout L = split_layout(num_seqs, total_tokens, num_v_heads, use_rows, true);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_ring_mu);   // one ring user enqueues at a time
+  RingState& R = g_ring[dev];
+  if (!R.ptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_prefill_ring);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(prefill record ring)");
+    e = cudaEventCreateWithFlags(&R.done, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate(record ring)");
+    R.ptr = ptr;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(st, &cap);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  const bool handoff = cap == cudaStreamCaptureStatusNone;
+  if (handoff && R.recorded && (e = cudaStreamWaitEvent(st, R.done, 0)) != cudaSuccess)
+    return cuda_fail(e, "cudaStreamWaitEvent(record ring)");
+  SplitParams sp = split_params(p, R.ptr, L, num_seqs, 0);
+  sp.ring_rows = static_cast<int>(use_rows);
+  if (use_rows >= L.max_chunks)
+    launch_two_stage(sp, tq, tk, tv, L, num_seqs, total_tokens, num_v_heads, st);
+  else
+    launch_windows(sp, tq, tk, tv, L, num_seqs, num_v_heads, st);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill (record ring) launch");
+  if (handoff) {
+    if ((e = cudaEventRecord(R.done, st)) != cudaSuccess)
+      return cuda_fail(e, "cudaEventRecord(record ring)");
+    R.recorded = true;
+  }
+  return GDN_B200_OK;
+}
+
+extern "C" int gdn_b200_prefill_fused(const void* q, const void* k, const void* v,
+                                      const float* state,
                                 const float* A_log, const void* a, const float* dt_bias,
                                 const void* b, const void* cu_seqlens,
                                 int32_t cu_seqlens_is_int64, double scale, void* output,
@@ -780,4 +935,4 @@ extern "C" int gdn_b200_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
   return GDN_B200_OK;
 }
 
-extern "C" int32_t gdn_b200_abi_version(void) { return 101; }
+extern "C" int32_t gdn_b200_abi_version(void) { return 102; }

@@ -28,7 +28,8 @@
 // folded tiles Q' and P' round once more to bf16 than the single-kernel path.
 // The workspace holds the tables and one 49 KiB record per (chunk, v-head);
 // it is caller-provided (gdn_b200_prefill_workspace_size), 256-byte aligned
-// (records sit at 1 KiB multiples from its start).
+// (records sit at 1 KiB multiples from its start), or the library's static
+// record ring, which holds the records of two windows of chunks at a time.
 #pragma once
 
 #include "prefill_kernel.cuh"
@@ -49,20 +50,27 @@ constexpr uint32_t kRecOffGam = 49152;     // gamma[64], 256 B
 constexpr uint32_t kRecBytes = 50176;      // 49 KiB (keeps records 1 KiB aligned)
 
 struct SplitLayout {
-  size_t off_header, off_seq, off_table, off_rec, total;
+  size_t off_header, off_seq, off_table, off_win, off_rec, total;
   long long max_chunks;
 };
 
+// Tables plus `rec_rows` rows of H_v records (rec_rows < 0: one row per chunk
+// of the table, every record of the call resident at once).  `windows`: room
+// for the per-window sequence ranges of an interleaved table.
 __host__ __device__ inline SplitLayout split_layout(long long num_seqs, long long total_tokens,
-                                                    int h_v) {
+                                                    int h_v, long long rec_rows = -1,
+                                                    bool windows = false) {
   SplitLayout L;
   L.max_chunks = (total_tokens + kChunk - 1) / kChunk + num_seqs;
   auto up = [](size_t x, size_t a) { return (x + a - 1) / a * a; };
   L.off_header = 0;
   L.off_seq = 256;
   L.off_table = up(L.off_seq + static_cast<size_t>(num_seqs + 1) * 4, 1024);
-  L.off_rec = up(L.off_table + static_cast<size_t>(L.max_chunks) * sizeof(ChunkInfo), 1024);
-  L.total = L.off_rec + static_cast<size_t>(L.max_chunks) * h_v * kRecBytes;
+  L.off_win = up(L.off_table + static_cast<size_t>(L.max_chunks) * sizeof(ChunkInfo), 256);
+  L.off_rec = up(L.off_win + (windows ? static_cast<size_t>(L.max_chunks) * 2 * sizeof(int) : 0),
+                 1024);
+  const long long rows = rec_rows < 0 ? L.max_chunks : rec_rows;
+  L.total = L.off_rec + static_cast<size_t>(rows) * h_v * kRecBytes;
   return L;
 }
 
@@ -72,19 +80,75 @@ struct SplitParams {
   int* header;            // [0] = total chunks
   int* seq_off;           // [N + 1] first chunk of each sequence
   ChunkInfo* table;       // [max_chunks]
-  uint8_t* records;       // [max_chunks][H_v] x kRecBytes
+  uint8_t* records;       // [ring_rows][H_v] x kRecBytes
   int num_seqs;
   int max_chunks;
+  // Records of table chunk g live in row g % ring_rows (ring_rows = max_chunks:
+  // one row per chunk; fewer: a ring that consecutive windows reuse).
+  int ring_rows;
   // Prep kernel: launched to follow the chunk-table kernel (programmatic
   // serialization), so it waits for that grid before reading the table.
   int wait_table;
-  // Chunk window [c_lo, c_hi): the prep kernel does the items of table chunks
-  // in it, the chain kernel the chunks of each sequence in it (index within
-  // the sequence).  The whole call is [0, INT_MAX); a one-sequence call split
-  // into pieces runs one window per piece (chunk c of the only sequence is
-  // table chunk c).
+  // Chunk window [c_lo, c_hi) of table (global) chunk indices: the prep kernel
+  // does the items of those chunks, the chain kernel those chunks of every
+  // sequence.  The whole call is [0, INT_MAX).  A sequence whose first chunk
+  // lies before the window continues from new_state, where the previous
+  // window left it.
   int c_lo, c_hi;
+  // Table order.  group = 1: sequence-major (sequence i's chunks at
+  // seq_off[i] ..).  group > 1: the chunks of each group of `group`
+  // consecutive sequences occupy the same span as in sequence-major order but
+  // are interleaved in rounds: round r holds chunks [r block, (r + 1) block)
+  // of every member, member by member.  A window then holds chunks of all the
+  // members of a group, each a consecutive run of its own chunks.
+  int group, block;
+  // Windows of an interleaved table: `window` chunks each (0: none).  The
+  // chunk-table kernel writes, per window w, the range [win_seq[2 w],
+  // win_seq[2 w + 1]) of sequences whose groups overlap it.  With scan set,
+  // CTA row blockIdx.y of the chain kernel runs the candidates of window
+  // c_lo / window: the range's first sequence + blockIdx.y, + gridDim.y, ...;
+  // otherwise CTA row y runs sequence y.
+  int window;
+  int scan;
+  int* win_seq;           // [2 x ceil(max_chunks / window)]
 };
+
+constexpr int kMaxGroup = 16;
+
+__device__ __forceinline__ uint8_t* record_at(const SplitParams& sp, int g, int head) {
+  // (no division unless the rows wrap: this sits on the producer's path)
+  const int row = g < sp.ring_rows ? g : g % sp.ring_rows;
+  return sp.records + (static_cast<size_t>(row) * sp.base.h_v + head) * kRecBytes;
+}
+
+// A sequence's group: the table span of the group and the members' chunk
+// counts (read from seq_off as needed; no per-thread array).
+struct GroupView {
+  int g0, base, members, rank, n;   // first member, span start, members, rank of this one, its chunks
+};
+
+__device__ inline GroupView group_view(const SplitParams& sp, int seq) {
+  GroupView g;
+  g.g0 = sp.group > 1 ? seq - seq % sp.group : seq;
+  g.members = sp.group > 1 ? min(sp.group, sp.num_seqs - g.g0) : 1;
+  g.rank = seq - g.g0;
+  g.base = sp.seq_off[g.g0];
+  g.n = sp.seq_off[seq + 1] - sp.seq_off[seq];
+  return g;
+}
+
+// Table position of chunk j of the sequence of `g` (increasing in j).
+__device__ inline int chunk_pos(const SplitParams& sp, const GroupView& g, int j) {
+  if (sp.group <= 1) return g.base + j;
+  const int rb = (j / sp.block) * sp.block;          // first chunk of j's round
+  int pos = g.base + (j - rb);
+  for (int m = 0; m < g.members; ++m) {
+    const int nm = sp.seq_off[g.g0 + m + 1] - sp.seq_off[g.g0 + m];
+    pos += min(nm, rb);                                          // the rounds before
+    if (m < g.rank) pos += min(sp.block, max(0, nm - rb));      // earlier members, this round
+  }
+  return pos;
+}
 
 // Programmatic dependent launch.  launch_dependents lets the grid launched
 // after this one with programmatic stream serialization start once every CTA
@@ -167,6 +231,7 @@ __global__ void __launch_bounds__(kTableThreads) gdn_chunk_table_kernel(SplitPar
     sp.seq_off[sp.num_seqs] = total;
     sp.header[0] = total;
   }
+  __syncthreads();   // pass 2 reads the chunk counts of a sequence's whole group
   for (int i = tid; i < sp.num_seqs; i += kTableThreads) {
     if (overflow) {   // overlapping sequences: all are treated as empty
       sp.seq_off[i] = 0;
@@ -174,14 +239,44 @@ __global__ void __launch_bounds__(kTableThreads) gdn_chunk_table_kernel(SplitPar
     }
     long long s0, s1;
     seq_range(p, i, s0, s1);
-    const int excl = sp.seq_off[i];
+    const GroupView g = group_view(sp, i);
     const int n = static_cast<int>((s1 - s0 + kChunk - 1) / kChunk);
-    for (int k = 0; k < n; ++k) {
-      ChunkInfo c;
-      c.seq = i;
-      c.cstart = s0 + static_cast<long long>(k) * kChunk;
-      c.clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - c.cstart));
-      sp.table[excl + k] = c;
+    const int run = sp.group > 1 ? sp.block : max(n, 1);   // chunks at consecutive positions
+    for (int k0 = 0; k0 < n; k0 += run) {
+      const int pos = chunk_pos(sp, g, k0);
+      for (int k = k0; k < min(n, k0 + run); ++k) {
+        ChunkInfo c;
+        c.seq = i;
+        c.cstart = s0 + static_cast<long long>(k) * kChunk;
+        c.clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - c.cstart));
+        sp.table[pos + (k - k0)] = c;
+      }
+    }
+  }
+  // Windows of an interleaved table: the sequences of the groups that
+  // overlap each window (windows past the table's end get an empty range).
+  if (sp.window > 0) {
+    const int groups = (sp.num_seqs + sp.group - 1) / sp.group;
+    auto group_of = [&](int c) {   // the last group whose span starts at or before c
+      int lo = 0, hi = groups - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sp.seq_off[mid * sp.group] <= c) lo = mid;
+        else hi = mid - 1;
+      }
+      return lo;
+    };
+    const int nwin = (sp.max_chunks + sp.window - 1) / sp.window;
+    for (int w = tid; w < nwin; w += kTableThreads) {
+      const long long c0 = static_cast<long long>(w) * sp.window;
+      int s_lo = 0, s_hi = 0;
+      if (c0 < total) {
+        const int c1 = static_cast<int>(min(c0 + sp.window, static_cast<long long>(total))) - 1;
+        s_lo = group_of(static_cast<int>(c0)) * sp.group;
+        s_hi = min(sp.num_seqs, (group_of(c1) + 1) * sp.group);
+      }
+      sp.win_seq[2 * w] = s_lo;
+      sp.win_seq[2 * w + 1] = s_hi;
     }
   }
   // Table slots past the last chunk get clen = 0: the prep kernel's CTAs for
@@ -517,7 +612,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     // A thread of the last warp issues them, off warp 0's path to the next
     // item's first product.
     if (tid == kP1StoreTid) {
-      uint8_t* rec = sp.records + (static_cast<size_t>(gc) * p.h_v + head) * kRecBytes;
+      uint8_t* rec = record_at(sp, gc, head);
       bulk_store(rec + kRecOffQW, qkw, 32768);
       bulk_store(rec + kRecOffP, tpzt + 16384, 8192);
       bulk_store(rec + kRecOffTb, tpzt + kP1TbOff, 8192);
@@ -619,7 +714,9 @@ __device__ __forceinline__ void state_sync(int id) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(32 * kC2StateWarps) : "memory");
 }
 
-template <int kVS>
+// kScan: the window form (CTA rows run a window's candidate sequences in turn);
+// otherwise CTA row y runs sequence y once.
+template <int kVS, bool kScan>
 __global__ void __launch_bounds__(kC2Threads, 1)
     gdn_prefill_chain_kernel(const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const SplitParams sp) {
@@ -630,42 +727,72 @@ __global__ void __launch_bounds__(kC2Threads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const PrefillParams& p = sp.base;
   const int head = blockIdx.x / (kHeadDim / kVS), vs = blockIdx.x % (kHeadDim / kVS);
-  const int seq = blockIdx.y;
   const int hq = head / (p.h_v / p.h_qk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_launch_dependents();   // a prep grid of the next piece may take the other SMs
-  const int seq_c0 = sp.seq_off[seq];
-  const int seq_n = sp.seq_off[seq + 1] - seq_c0;
-  const int win_lo = min(sp.c_lo, seq_n), win_hi = min(sp.c_hi, seq_n);
-  const int gc0 = seq_c0 + win_lo;   // this call's first chunk of the sequence
-  const int nch = win_hi - win_lo;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + L::kOffTmemPtr);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
+  // TMEM is allocated by the first sequence that has chunks here (after its
+  // table lookups, so the allocation overlaps nothing on the critical path)
+  // and kept for the CTA's later sequences.
+  uint32_t tmem = 0;
+  bool have_tmem = false;
+
+  // One sequence's chunks of the window.  Returns false once a wait has run out
+  // (the CTA then stops).  Every early return is CTA-uniform.
+  auto run_sequence = [&](const int seq) -> bool {
+  const GroupView gv = group_view(sp, seq);
+  const int seq_n = gv.n;
+  // this window's chunks of the sequence: j in [j0, j0 + nch) (table
+  // positions increase with j)
+  auto first_pos_at_or_after = [&](int c) {
+    int lo = 0, hi = seq_n;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (chunk_pos(sp, gv, mid) >= c) hi = mid;
+      else lo = mid + 1;
+    }
+    return lo;
+  };
+  const int j0 = first_pos_at_or_after(sp.c_lo);
+  const int nch = first_pos_at_or_after(sp.c_hi) - j0;
   // this CTA's slice: state rows v in [kVS vs, kVS vs + kVS)
   const size_t sbase = (static_cast<size_t>(seq) * p.h_v + head) * kHeadDim * kHeadDim +
                        static_cast<size_t>(kVS * vs) * kHeadDim;
 
-  if (nch <= 0) {   // ref kernel_prefill.cu:61-66: the state passes through unchanged
-    float4* dst = reinterpret_cast<float4*>(p.new_state + sbase);
-    const float4* src = p.state ? reinterpret_cast<const float4*>(p.state + sbase) : nullptr;
-    for (int i = tid; i < kVS * kHeadDim / 4; i += kC2Threads)
-      dst[i] = src ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    return;
+  if (seq_n == 0) {   // ref kernel_prefill.cu:61-66: the state passes through unchanged
+    if (sp.c_lo == 0) {     // (once: in the first window)
+      float4* dst = reinterpret_cast<float4*>(p.new_state + sbase);
+      const float4* src = p.state ? reinterpret_cast<const float4*>(p.state + sbase) : nullptr;
+      for (int i = tid; i < kVS * kHeadDim / 4; i += kC2Threads)
+        dst[i] = src ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    return true;
   }
+  if (nch <= 0) return true;   // none of this sequence's chunks lies in the window
+  const float* init = j0 == 0 ? p.state : p.new_state;
   // Chunks of one sequence are consecutive 64-token windows; only the last
   // may be short.
-  const long long cstart0 = sp.table[gc0].cstart;
-  const int clen_last = sp.table[gc0 + nch - 1].clen;
+  const long long cstart0 = sp.table[chunk_pos(sp, gv, j0)].cstart;
+  const int clen_last = sp.table[chunk_pos(sp, gv, j0 + nch - 1)].clen;
   auto chunk_len = [&](int c) { return c == nch - 1 ? clen_last : kChunk; };
-
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + L::kOffTmemPtr);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
+  // Table position of window chunk c, for the producer, which asks in order:
+  // positions run consecutively within a round of sp.block chunks.
+  int pos_c = -1, pos_v = 0;
+  auto table_pos = [&](int c) {
+    if (sp.group <= 1) return gv.base + j0 + c;
+    if (pos_c >= 0 && c == pos_c + 1 && (j0 + c) % sp.block != 0) pos_v += 1;
+    else pos_v = chunk_pos(sp, gv, j0 + c);
+    pos_c = c;
+    return pos_v;
+  };
 
   auto load_a = [&](int c) {   // record tiles + V of chunk c -> stage c & 1
     const int st = c & 1;
     uint8_t* stage = smem + st * L::kStage;
     uint64_t* bar = bars + kC2BarLdA + st;
-    const uint8_t* rec =
-        sp.records + (static_cast<size_t>(gc0 + c) * p.h_v + head) * kRecBytes;
+    const uint8_t* rec = record_at(sp, table_pos(c), head);
     mbar_arrive_expect_tx(bar, sp.zero_v ? L::kLoadA - 8192 * L::kVBlocks : L::kLoadA);
     bulk_load(stage + L::kStQW, rec + kRecOffQW, 32768, bar);
     bulk_load(stage + L::kStPT, rec + kRecOffP, 16384, bar);
@@ -687,12 +814,14 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     tma_load_3d(stage + L::kStK + 8192, &tm_k, bar, 64, hq, t0);
   };
 
-  if (warp == 0) {
+  if (!have_tmem && warp == 0) {
     tmem_alloc(tmem_ptr, L::kTmCols);
     tmem_relinquish();
   }
+  // (re)initialised per sequence: every phase of the previous sequence has
+  // completed and been waited for before the barrier that ended it
   if (warp == kC2LoaderWarp && lane == 0) {
-    *abort_flag = 0;
+    if (!have_tmem) *abort_flag = 0;
     for (int i = 0; i < kC2NumBars; ++i)
       mbar_init(bars + i, (i == kC2BarOut || i == kC2BarOut + 1) ? kC2OutWarps : 1);
     fence_mbarrier_init();
@@ -720,15 +849,17 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   if (warp < kC2StateWarps) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j)
-      sreg[j] =
-          p.state ? p.state[sbase + static_cast<size_t>(kCols * half + j) * kHeadDim + row] : 0.f;
+      sreg[j] = init ? init[sbase + static_cast<size_t>(kCols * half + j) * kHeadDim + row] : 0.f;
     st_cols_bf16(smem + L::kOffSB, 16384, row, sreg, 1.0f);
     fence_proxy_async_smem();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_ptr;
+  if (!have_tmem) {
+    tmem = *tmem_ptr;
+    have_tmem = true;
+  }
   const uint32_t tm_lane = static_cast<uint32_t>(quad * 32) << 16;
   const uint32_t idesc_uo = idesc_bf16_f32(128, kVS, 0, 1);
 
@@ -955,12 +1086,30 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (!*abort_flag && warp < kC2StateWarps) {
+  const bool aborted = *abort_flag != 0;
+  if (!aborted && warp < kC2StateWarps) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j)
       p.new_state[sbase + static_cast<size_t>(kCols * half + j) * kHeadDim + row] = sreg[j];
   }
-  if (warp == 0) tmem_dealloc(tmem, L::kTmCols);
+  return !aborted;
+  };
+
+  if constexpr (kScan) {
+    const int w = sp.c_lo / sp.window;
+    const int s_end = sp.win_seq[2 * w + 1];
+    for (int seq = sp.win_seq[2 * w] + static_cast<int>(blockIdx.y); seq < s_end;
+         seq += static_cast<int>(gridDim.y))
+      if (!run_sequence(seq)) break;
+  } else {
+    run_sequence(static_cast<int>(blockIdx.y));
+  }
+  if (have_tmem) {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, L::kTmCols);
+  }
 }
 
 }  // namespace gdn

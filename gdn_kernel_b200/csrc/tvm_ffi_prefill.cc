@@ -3,8 +3,6 @@
 // exported there with TVM_FFI_DLL_EXPORT_TYPED_FUNC(kernel, GDNPrefillKernel)).
 // Same argument order; cu_seqlens may be int32 or int64 (the reference reads
 // int64 only, kernel_prefill.cu:323).
-#include <cuda_runtime.h>
-
 #include "tvm_ffi_common.h"
 
 namespace gdn_tvm {
@@ -31,25 +29,16 @@ void GdnPrefill(TensorView q, TensorView k, TensorView v, TensorView state, Tens
   check_tensor(output, "output", kDLBfloat, 16, {T, H_v, D}, dev);
   check_tensor(new_state, "new_state", kDLFloat, 32, {N, H_v, D, D}, dev);
   const float* st = optional_state(state, "state", {N, H_v, D, D}, dev);
-  // The reference signature carries no workspace: take the two-stage path's
-  // workspace from the stream-ordered pool of this device and give it back on
-  // the same stream, so the call stays asynchronous.
+  // The reference signature carries no workspace, and gdn_b200_prefill needs
+  // none: it works in the library's static record ring (no allocation).
   DeviceGuard guard(dev);
-  cudaStream_t stream = static_cast<cudaStream_t>(env_stream(dev));
-  const uint64_t ws_bytes = gdn_b200_prefill_workspace_size(N, T, static_cast<int32_t>(H_v));
-  void* ws = nullptr;
-  if (ws_bytes > 0) {
-    cudaError_t e = cudaMallocAsync(&ws, ws_bytes, stream);
-    if (e != cudaSuccess) TVM_FFI_THROW(RuntimeError) << "workspace: " << cudaGetErrorString(e);
-  }
-  const int rc = gdn_b200_prefill_ws(ptr(q), ptr(k), ptr(v), st,
-                                     static_cast<const float*>(ptr(A_log)), ptr(a),
-                                     static_cast<const float*>(ptr(dt_bias)), ptr(b),
-                                     ptr(cu_seqlens), cu64 ? 1 : 0, scale, ptr(output),
-                                     static_cast<float*>(ptr(new_state)), N, T,
-                                     static_cast<int32_t>(H_qk), static_cast<int32_t>(H_v),
-                                     static_cast<int32_t>(D), ws, ws_bytes, stream);
-  if (ws) cudaFreeAsync(ws, stream);
+  const int rc = gdn_b200_prefill(ptr(q), ptr(k), ptr(v), st,
+                                  static_cast<const float*>(ptr(A_log)), ptr(a),
+                                  static_cast<const float*>(ptr(dt_bias)), ptr(b),
+                                  ptr(cu_seqlens), cu64 ? 1 : 0, scale, ptr(output),
+                                  static_cast<float*>(ptr(new_state)), N, T,
+                                  static_cast<int32_t>(H_qk), static_cast<int32_t>(H_v),
+                                  static_cast<int32_t>(D), env_stream(dev));
   check_rc(rc);
 }
 

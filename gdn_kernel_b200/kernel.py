@@ -207,7 +207,7 @@ def state_affine(state, transfer, offset, out=None):
     return out
 
 
-PREFILL_PATHS = ("split", "fused")
+PREFILL_PATHS = ("split", "ring", "fused")
 
 
 def prefill_workspace_bytes(num_seqs: int, total_tokens: int, num_v_heads: int) -> int:
@@ -227,8 +227,11 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
     ``path="split"`` (default) runs the two-stage kernels (parallel per-chunk
     preparation, then the sequential state recurrence) with a device workspace
     (``workspace``: a uint8 CUDA tensor of at least ``prefill_workspace_bytes``
-    bytes, allocated here when omitted); ``path="fused"`` runs the single
-    kernel that needs no workspace.  Both give the same results.
+    bytes, allocated here when omitted); ``path="ring"`` runs the same kernels
+    in the library's static record ring and allocates nothing (the C ABI's
+    ``gdn_b200_prefill``, what the TVM-FFI ``kernel`` calls; bit-identical to
+    "split"); ``path="fused"`` runs the single kernel that needs no workspace
+    (agrees with the others to the prefill tolerance).
     """
     dev = _cuda_device(q)
     _require(q.dim() == 3 and v.dim() == 3, "q and v must be packed [T, H, D]")
@@ -255,7 +258,10 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
     args = (_ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b),
             _ptr(cu_seqlens), 1 if cu_seqlens.dtype == torch.int64 else 0, float(scale or 0.0),
             _ptr(output), _ptr(new_state), N, T, h_qk, h_v, D)
-    if path == "fused" or N == 0:
+    if path == "fused":
+        _launch(dev, lib.gdn_b200_prefill_fused, *args)
+        return
+    if path == "ring" or N == 0:
         _launch(dev, lib.gdn_b200_prefill, *args)
         return
     need = prefill_workspace_bytes(N, T, h_v)

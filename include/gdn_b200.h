@@ -90,12 +90,28 @@ int gdn_b200_decode_pool(const void* q, const void* k, const void* v,
                          int64_t pool_size, int32_t num_qk_heads, int32_t num_v_heads,
                          int32_t head_dim, void* stream);
 
+/* Capacity (bytes) of the record ring that gdn_b200_prefill works in. */
+#define GDN_B200_PREFILL_RING_BYTES (128ull << 20)
+
 /*
  * Chunked (C=64) prefill over `num_seqs` packed variable-length sequences.
  * Replaces the reference's TVM-FFI `kernel` of solution/cuda/kernel_prefill.cu:300-339
  * (GDNPrefillKernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
  * new_state)).  `cu_seqlens` is device memory of int32 (cu_seqlens_is_int64 = 0) or
  * int64 (= 1) entries; `total_tokens` is the packed token extent T of q/k/v/a/b/output.
+ *
+ * Like the reference kernel it allocates nothing.  It runs the two-stage path
+ * of gdn_b200_prefill_ws in a record ring that is part of this library's
+ * device image (GDN_B200_PREFILL_RING_BYTES on every GPU that loads the
+ * library, held until the process exits): when the problem's records do not
+ * all fit, consecutive windows of chunks take turns in the ring.  Results are
+ * bit-identical to gdn_b200_prefill_ws.  Calls on one device share the ring;
+ * each call's stream waits (on the GPU, through an event) for the previous
+ * call's kernels, so calls from several streams or threads are safe, except
+ * under CUDA graph capture, where that handoff is skipped and captured calls
+ * must not overlap other calls on the device.  A problem whose chunk tables
+ * ((ceil(T/64) + N) x 16 bytes) crowd out two rows of records is rejected with
+ * GDN_B200_ERR_INVALID_ARGUMENT.
  */
 int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* state,
                      const float* A_log, const void* a, const float* dt_bias, const void* b,
@@ -103,6 +119,23 @@ int gdn_b200_prefill(const void* q, const void* k, const void* v, const float* s
                      void* output, float* new_state,
                      int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
                      int32_t num_v_heads, int32_t head_dim, void* stream);
+
+/*
+ * The same prefill as one kernel: one CTA per (sequence, v-head) walks its
+ * chunks and does each chunk's preparation inline before its recurrence, as
+ * the reference kernel's structure does (ref solution/cuda/kernel_prefill.cu:36-298,
+ * entry point :300-339).  It needs no workspace at all, but puts all the
+ * per-chunk work on the sequential chain (several times slower than the
+ * two-stage path for long sequences).  Same arguments and semantics as
+ * gdn_b200_prefill; results agree with it to the prefill tolerance, not bitwise
+ * (the two paths fold the products differently).
+ */
+int gdn_b200_prefill_fused(const void* q, const void* k, const void* v, const float* state,
+                           const float* A_log, const void* a, const float* dt_bias,
+                           const void* b, const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                           double scale, void* output, float* new_state, int64_t num_seqs,
+                           int64_t total_tokens, int32_t num_qk_heads, int32_t num_v_heads,
+                           int32_t head_dim, void* stream);
 
 /*
  * Bytes of device workspace gdn_b200_prefill_ws needs for this problem size
@@ -115,7 +148,8 @@ uint64_t gdn_b200_prefill_workspace_size(int64_t num_seqs, int64_t total_tokens,
 
 /*
  * Same contract and results as gdn_b200_prefill (replaces the same reference
- * entry point, solution/cuda/kernel_prefill.cu:300-339), computed in two stages:
+ * entry point, solution/cuda/kernel_prefill.cu:300-339) with every record of the
+ * call resident in a caller workspace, computed in two stages:
  * the S-independent work of every (chunk, v-head) in parallel across the GPU,
  * then the sequential state recurrence per (sequence, v-head, 64-column V
  * slice).  `workspace` is caller-owned device memory of at least

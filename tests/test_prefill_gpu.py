@@ -256,3 +256,77 @@ def test_unordered_cu_seqlens_flagged_and_bounded():
     torch.cuda.synchronize()
     assert _lib.device_status(torch.cuda.current_device()) == _lib.STATUS_BAD_SEQLENS
     assert torch.count_nonzero(ns2[1]) == 0
+
+
+RING_CASES = [
+    ([150, 0, 64, 33], True, False),       # records fit the ring: one window
+    ([8192], False, False),                # one sequence over four ring windows
+    ([12000], True, True),                 # in place, six windows
+    ([3000, 0, 5000, 4000, 1], True, False),   # windows that span sequence boundaries
+]
+
+
+@pytest.mark.parametrize("lengths,with_state,in_place", RING_CASES)
+def test_ring_path_bitwise_equal_to_workspace(lengths, with_state, in_place):
+    """gdn_b200_prefill works in the library's static record ring (no
+    allocation), in windows of chunks when the records do not all fit.  Every
+    chunk computes the same products from the same tiles as with a caller
+    workspace, and the state crosses window boundaries in fp32, so the results
+    are bit-identical."""
+    x = W.make_prefill_inputs(lengths, seed=51, device="cuda", with_state=with_state)
+    st1 = x.state.clone() if with_state else None
+    st2 = x.state.clone() if with_state else None
+    o1, s1 = K.prefill(x.q, x.k, x.v, st1, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale,
+                       in_place=in_place, path="ring")
+    o2, s2 = K.prefill(x.q, x.k, x.v, st2, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale,
+                       in_place=in_place, path="split")
+    torch.cuda.synchronize()
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+    assert torch.equal(o1, o2)
+    assert torch.equal(s1, s2)
+
+
+def test_ring_path_matches_oracle_over_windows():
+    """Five ring windows (a 6,000-token sequence after a short one) against the
+    fp32 oracle."""
+    lengths = [100, 6000]
+    x = W.make_prefill_inputs(lengths, seed=52)
+    out, ns = _run(x, "ring")
+    ro, rs = _oracle(x)
+    assert_prefill_close(out, ns, ro, rs, lengths)
+
+
+def test_ring_path_calls_on_two_streams():
+    """Calls on two streams share the ring; the second call's stream waits for
+    the first call's kernels on the GPU, so both results are right."""
+    xa = W.make_prefill_inputs([7000], seed=53, device="cuda")
+    xb = W.make_prefill_inputs([2000, 4500], seed=54, device="cuda")
+    ref = [K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale,
+                     path="split") for x in (xa, xb)]
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    res = []
+    for x, s in ((xa, s1), (xb, s2)):
+        with torch.cuda.stream(s):
+            res.append(K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b,
+                                 x.cu_seqlens, x.scale, path="ring"))
+    torch.cuda.synchronize()
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+    for (o, s), (ro, rs) in zip(res, ref):
+        assert torch.equal(o, ro)
+        assert torch.equal(s, rs)
+
+
+def test_ring_path_interleaved_groups():
+    """Several sequences whose records overflow the ring: the chunk table
+    interleaves groups of sequences so that each ring window holds a run of
+    chunks of every group member (group and round sizes from the window size).
+    Bit-identical to the workspace path, and within tolerance of the oracle."""
+    lengths = [700, 3000, 1, 2500, 4100, 0, 1800, 640, 5000]
+    x = W.make_prefill_inputs(lengths, seed=55)
+    o1, s1 = _run(x, "ring")
+    o2, s2 = _run(x, "split")
+    assert torch.equal(o1, o2)
+    assert torch.equal(s1, s2)
+    ro, rs = _oracle(x)
+    assert_prefill_close(o1, s1, ro, rs, lengths)

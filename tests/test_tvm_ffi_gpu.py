@@ -5,7 +5,7 @@ launch the same kernels on the same inputs, so the results agree bit for bit."""
 import pytest
 import torch
 
-from helpers import DECODE_OUT_TOL, DECODE_STATE_TOL, assert_prefill_close
+from helpers import assert_prefill_close
 from gdn_kernel_b200 import kernel as K, workloads as W
 
 pytestmark = pytest.mark.gpu
@@ -33,7 +33,31 @@ def test_tvm_prefill_kernel_matches_capi():
     tvm_kernel(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale, out, ns)
     ro, rs = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale)
     torch.cuda.synchronize()
+    assert torch.equal(out, ro)
+    assert torch.equal(ns, rs)
     assert_prefill_close(out.cpu(), ns.cpu(), ro.cpu(), rs.cpu(), lengths)
+
+
+def test_tvm_prefill_kernel_allocates_nothing():
+    """The drop-in `kernel` works in the library's static record ring: a call
+    that needs several ring windows (one 9,000-token sequence) leaves torch's
+    allocator untouched and matches the workspace path bit for bit."""
+    tvm_kernel = K.load_tvm_kernel("prefill")
+    x = W.make_prefill_inputs([9000], seed=5, device="cuda", cu_dtype=torch.int64)
+    out = torch.empty(9000, 32, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty_like(x.state)
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_stats()["allocation.all.allocated"]
+    free0, _ = torch.cuda.mem_get_info()
+    tvm_kernel(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale, out, ns)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_stats()["allocation.all.allocated"] == before
+    assert free1 == free0
+    ro, rs = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ro)
+    assert torch.equal(ns, rs)
 
 
 def test_tvm_prefill_rejects_bad_dtype():
