@@ -66,6 +66,10 @@ _SIGNATURES = {
     "gdn_b200_device_status": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32),
                                               ctypes.c_int32]),
     "gdn_b200_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _P]),
+    "gdn_b200_selftest_prefill_abort": (ctypes.c_int, [ctypes.c_uint64, _P, _P, _P, _P, _P,
+                                                       ctypes.c_int64, ctypes.c_int64,
+                                                       ctypes.c_int32, ctypes.c_int32,
+                                                       ctypes.c_int32, _P, ctypes.c_uint64, _P]),
     "gdn_b200_last_error": (ctypes.c_char_p, []),
     "gdn_b200_abi_version": (ctypes.c_int32, []),
 }

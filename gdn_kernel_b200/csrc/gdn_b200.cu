@@ -367,6 +367,8 @@ SplitParams split_params(const PrefillParams& p, void* workspace, const SplitLay
   sp.block = 1;
   sp.window = 0;
   sp.scan = 0;
+  sp.wait_limit_ns = 0;
+  sp.withhold_from = -1;
   sp.win_seq = reinterpret_cast<int*>(ws + L.off_win);
   sp.c_lo = 0;
   sp.c_hi = std::numeric_limits<int>::max();
@@ -759,13 +761,13 @@ extern "C" int gdn_b200_prefill_prepare(const void* q, const void* k, const floa
   return GDN_B200_OK;
 }
 
-extern "C" int gdn_b200_prefill_recur(const void* k, const void* v, const float* state,
-                                      double scale, void* output, float* new_state,
-                                      int64_t num_seqs, int64_t total_tokens,
-                                      int32_t num_qk_heads, int32_t num_v_heads,
-                                      int32_t head_dim, const void* workspace,
-                                      uint64_t workspace_bytes, void* stream) {
-  t_last_error.clear();
+namespace gdn {
+namespace {
+int recur_impl(const void* k, const void* v, const float* state, double scale, void* output,
+               float* new_state, int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+               int32_t num_v_heads, int32_t head_dim, const void* workspace,
+               uint64_t workspace_bytes, void* stream, unsigned long long wait_limit_ns,
+               int withhold_from) {
   if (int rc = check_two_stage(num_seqs, total_tokens, num_qk_heads, num_v_heads, head_dim,
                                workspace, workspace_bytes))
     return rc;
@@ -800,12 +802,41 @@ extern "C" int gdn_b200_prefill_recur(const void* k, const void* v, const float*
   p.h_v = num_v_heads;
   p.status = status;
   const SplitLayout L = split_layout(num_seqs, total_tokens, num_v_heads);
-  const SplitParams sp =
+  SplitParams sp =
       split_params(p, const_cast<void*>(workspace), L, num_seqs, v == nullptr ? 1 : 0);
+  sp.wait_limit_ns = wait_limit_ns;
+  sp.withhold_from = withhold_from;
   launch_recur(sp, tk, tv, num_seqs, num_v_heads, static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill recurrence launch");
   return GDN_B200_OK;
+}
+}  // namespace
+}  // namespace gdn
+
+extern "C" int gdn_b200_prefill_recur(const void* k, const void* v, const float* state,
+                                      double scale, void* output, float* new_state,
+                                      int64_t num_seqs, int64_t total_tokens,
+                                      int32_t num_qk_heads, int32_t num_v_heads,
+                                      int32_t head_dim, const void* workspace,
+                                      uint64_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  return recur_impl(k, v, state, scale, output, new_state, num_seqs, total_tokens, num_qk_heads,
+                    num_v_heads, head_dim, workspace, workspace_bytes, stream, 0, -1);
+}
+
+extern "C" int gdn_b200_selftest_prefill_abort(uint64_t limit_ns, const void* k, const void* v,
+                                               const float* state, void* output,
+                                               float* new_state, int64_t num_seqs,
+                                               int64_t total_tokens, int32_t num_qk_heads,
+                                               int32_t num_v_heads, int32_t head_dim,
+                                               const void* workspace, uint64_t workspace_bytes,
+                                               void* stream) {
+  t_last_error.clear();
+  if (limit_ns == 0 || limit_ns > 1000000000ull)
+    return fail(GDN_B200_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 1e9]");
+  return recur_impl(k, v, state, 0.0, output, new_state, num_seqs, total_tokens, num_qk_heads,
+                    num_v_heads, head_dim, workspace, workspace_bytes, stream, limit_ns, 2);
 }
 
 // ---------------------------------------------------------------- allocation-free prefill

@@ -105,13 +105,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // thread raised `abort`, -1 when this thread's own limit ran out (it then
 // raises `abort`).
 __device__ __forceinline__ int mbar_wait_or_abort(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort) {
+                                                  volatile int* abort,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return 1;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity)) return 1;
     if (*abort) return 0;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort = 1;
       return -1;
     }

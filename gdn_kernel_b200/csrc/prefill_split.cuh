@@ -111,6 +111,11 @@ struct SplitParams {
   int window;
   int scan;
   int* win_seq;           // [2 x ceil(max_chunks / window)]
+  // Failure-detection self-test of the chain kernel: a wait limit (0: the
+  // default kWaitLimitNs), and a chunk from which the producer issues no more
+  // loads (-1: none), so that a wait nothing will satisfy runs out.
+  unsigned long long wait_limit_ns;
+  int withhold_from;
 };
 
 constexpr int kMaxGroup = 16;
@@ -865,8 +870,9 @@ __global__ void __launch_bounds__(kC2Threads, 1)
 
   // Waits are warp-uniform: every lane polls, and the warp proceeds only if
   // all saw the phase complete (a limit that runs out mid-warp cannot split it).
+  const unsigned long long limit_ns = sp.wait_limit_ns ? sp.wait_limit_ns : kWaitLimitNs;
   auto warp_wait = [&](int bar, uint32_t parity, unsigned int code) {
-    const int r = mbar_wait_or_abort(bars + bar, parity, abort_flag);
+    const int r = mbar_wait_or_abort(bars + bar, parity, abort_flag, limit_ns);
     if (r < 0) atomicOr(p.status, code);
     return __all_sync(0xffffffffu, r == 1);
   };
@@ -885,6 +891,9 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     int issued = nch > 1 ? 2 : 1;
     bool ok = true;
     for (int c = 2; c < nch; ++c) {
+      // (self-test: no more loads; every issued one is consumed before the
+      // consumers' first wait on a withheld stage)
+      if (sp.withhold_from >= 2 && c >= sp.withhold_from) break;
       const int st = c & 1;
       if (!(ok = warp_wait(kC2BarFreeA + st, ((c - 2) >> 1) & 1, kStatusMmaTimeout))) break;
       if (elect_one()) load_a(c);

@@ -251,6 +251,26 @@ int gdn_b200_device_status(int32_t device, uint32_t* status, int32_t clear);
  */
 int gdn_b200_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
+/*
+ * Diagnostic of the chain kernel's failure handling: the recurrence of
+ * gdn_b200_prefill_recur (same arguments; scale 1/sqrt(D)) over a workspace a
+ * gdn_b200_prefill_prepare call filled, with every bounded wait of the chain
+ * kernel limited to `limit_ns` nanoseconds (at most 1 s), and with the loads of
+ * each sequence's chunks from its third one on withheld.  The first wait on a
+ * withheld stage runs out: that CTA raises its abort flag, every one of its
+ * roles leaves its loop, waits (bounded) for its copies and tensor-core
+ * operations in flight, the CTA frees its TMEM and returns, and the status
+ * word gets GDN_B200_STATUS_TMA_TIMEOUT (or _MMA_TIMEOUT).  Outputs and
+ * new_state are then incomplete; the context stays usable.  Sequences of at
+ * most two chunks (128 tokens) complete normally.  No counterpart in the
+ * reference.
+ */
+int gdn_b200_selftest_prefill_abort(uint64_t limit_ns, const void* k, const void* v,
+                                    const float* state, void* output, float* new_state,
+                                    int64_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                                    int32_t num_v_heads, int32_t head_dim, const void* workspace,
+                                    uint64_t workspace_bytes, void* stream);
+
 /* Message of the last failing call on this thread ("" if none). */
 const char* gdn_b200_last_error(void);
 
