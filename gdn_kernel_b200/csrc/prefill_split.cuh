@@ -749,8 +749,9 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   auto run_sequence = [&](const int seq) -> bool {
   const GroupView gv = group_view(sp, seq);
   const int seq_n = gv.n;
-  // this window's chunks of the sequence: j in [j0, j0 + nch) (table
-  // positions increase with j)
+  // this window's chunks of the sequence: j in [j0, j0 + nch).  Sequence-major
+  // tables hold them at gv.base + j; interleaved ones are searched (table
+  // positions increase with j).
   auto first_pos_at_or_after = [&](int c) {
     int lo = 0, hi = seq_n;
     while (lo < hi) {
@@ -760,8 +761,14 @@ __global__ void __launch_bounds__(kC2Threads, 1)
     }
     return lo;
   };
-  const int j0 = first_pos_at_or_after(sp.c_lo);
-  const int nch = first_pos_at_or_after(sp.c_hi) - j0;
+  int j0, nch;
+  if (sp.group <= 1) {
+    j0 = min(max(sp.c_lo - gv.base, 0), seq_n);
+    nch = min(max(sp.c_hi - gv.base, 0), seq_n) - j0;
+  } else {
+    j0 = first_pos_at_or_after(sp.c_lo);
+    nch = first_pos_at_or_after(sp.c_hi) - j0;
+  }
   // this CTA's slice: state rows v in [kVS vs, kVS vs + kVS)
   const size_t sbase = (static_cast<size_t>(seq) * p.h_v + head) * kHeadDim * kHeadDim +
                        static_cast<size_t>(kVS * vs) * kHeadDim;
