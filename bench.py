@@ -287,6 +287,72 @@ def time_decode_pool(K, batch, seq_len, steps, warmup, flush, state_dtype, inter
     return [e0.elapsed_time(e1) for e0, e1 in ev]
 
 
+def time_steady(calls, flush, replays=10, warmup=3):
+    """Device time (ms) per call of ``len(calls)`` calls run back to back, as a
+    serving loop issues its steps: captured once into a CUDA graph, the graph
+    replayed with the L2 flushed between replays.  Each call has its own inputs
+    and state, together larger than the L2, so no call finds another's data
+    cached; consecutive launches overlap only at their edges."""
+    for c in calls:
+        c()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for c in calls:
+            c()
+    for _ in range(warmup):
+        flush.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    ev = [_events() for _ in range(replays)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        g.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    ms = statistics.median([e0.elapsed_time(e1) for e0, e1 in ev]) / len(calls)
+    del g
+    return ms
+
+
+def steady_decode(K, hbm_peak, flush, n_sets=16):
+    """The decode serving forms back to back (time_steady): the reference decode
+    at B = 1, 8, 32, 64 and the pooled bf16 T=1 / fp32 T=4 decode at B=64."""
+    from gdn_kernel_b200 import workloads as W
+
+    res = {}
+    for b in (1, 8, 32, 64):
+        xs = [W.make_decode_inputs(b, seed=4000 + i, device="cuda") for i in range(n_sets)]
+        outs = [torch.empty(b, 1, H_V, D, dtype=torch.bfloat16, device="cuda") for _ in xs]
+        calls = [(lambda x=x, o=o: K.gdn_decode(x.q, x.k, x.v, x.state, x.A_log, x.a,
+                                                x.dt_bias, x.b, x.scale, o, x.state))
+                 for x, o in zip(xs, outs)]
+        ms = time_steady(calls, flush)
+        nbytes = b * STATE_BYTES_PER_SEQ
+        res[f"decode_B{b}"] = {"us_per_step": round(ms * 1e3, 2),
+                               "frac_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3)}
+        del xs, outs, calls
+    for name, seq_len, sdt in (("pool_B64_T1_bf16", 1, torch.bfloat16),
+                               ("pool_B64_T4_fp32", 4, torch.float32)):
+        xs = [W.make_pool_decode_inputs(64, seq_len, 64, seed=5000 + i, device="cuda",
+                                        state_dtype=sdt) for i in range(n_sets)]
+        outs = [torch.empty(64, seq_len, H_V, D, dtype=torch.bfloat16, device="cuda")
+                for _ in xs]
+        calls = [(lambda x=x, o=o: K.gdn_decode_pool(x.q, x.k, x.v, x.pool, x.indices, x.A_log,
+                                                     x.a, x.dt_bias, x.b, x.scale, o))
+                 for x, o in zip(xs, outs)]
+        ms = time_steady(calls, flush)
+        esz = 4 if sdt == torch.float32 else 2
+        nbytes = 64 * H_V * D * D * esz * 2
+        res[name] = {"us_per_step": round(ms * 1e3, 2),
+                     "frac_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3)}
+        del xs, outs, calls
+    res["method"] = (f"{n_sets} steps on distinct inputs and states captured in one CUDA graph, "
+                     "L2 flushed between replays; device time per step")
+    return res
+
+
 def time_decode_e2e(K, batch, steps, warmup, flush, seed=0):
     """Decode through the C ABI with pinned host inputs/outputs each step."""
     from gdn_kernel_b200 import workloads as W
@@ -588,7 +654,7 @@ def time_context_parallel(K, rank, world, flush, total_tokens, iters=3, warmup=1
     import torch.distributed as dist
 
     x = W.make_prefill_inputs([total_tokens], seed=6100, device="cuda")
-    lo, hi = CP.cp_segments(total_tokens, world)[rank]
+    lo, hi = CP.cp_segments(total_tokens, world, CP.FIRST_SEGMENT_WEIGHT)[rank]
     if world == 1:
         out = torch.empty(total_tokens, H_V, D, dtype=torch.bfloat16, device="cuda")
         ns = torch.empty(1, H_V, D, D, dtype=torch.float32, device="cuda")
@@ -625,8 +691,9 @@ def time_context_parallel(K, rank, world, flush, total_tokens, iters=3, warmup=1
             "tokens_per_s": round(total_tokens / (ms * 1e-3), 1),
             "segment_tokens_this_rank": hi - lo,
             "method": "single call (one sequence in overlapping pieces)" if world == 1 else
-                      f"context-parallel over {world} ranks (rank 0 runs its segment, middle "
-                      f"ranks pass A, all-gather of the affine maps, pass B)"}
+                      f"context-parallel over {world} ranks (rank 0 runs its segment; the "
+                      f"others run pass A, two concurrent recurrences; all-gather of the "
+                      f"affine maps; fold; output correction GEMM)"}
 
 
 def prefill_hbm_bytes(lengths, with_state):
@@ -728,6 +795,8 @@ def run_gpu(args, rank, world, local_rank, traffic=None):
                           "state_GBps": round(nbytes / (ms * 1e-3) / 1e9, 1),
                           "frac_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3)}
         extra["decode_pool"] = pool
+        # ---- the same forms back to back, as a serving loop runs them
+        extra["decode_steady"] = steady_decode(K, hbm_peak, flush)
         # ---- prefill configs[2] and configs[3]
         from gdn_kernel_b200 import workloads as W
         pre, cases = {}, {}

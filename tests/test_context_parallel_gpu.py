@@ -60,48 +60,70 @@ def test_kernel_segment_maps_match_function_maps():
     through one packed prefill call, and both are the segment's affine map."""
     x = W.make_prefill_inputs([700], seed=23, device="cuda")
     args = (x.q, x.k, x.v, x.A_log, x.a, x.dt_bias, x.b, x.scale)
-    m1, n1 = CP._KernelSegment(*args).maps()
-    m2, n2 = CP.segment_affine(*args)
+    seg = CP._KernelSegment(*args)
+    m1, n1 = seg.pass_a()
+    m2, n2, o2, q2 = CP.segment_pass_a(*args)
     torch.cuda.synchronize()
     torch.testing.assert_close(m1, m2, atol=1e-6, rtol=1e-5)
     torch.testing.assert_close(n1, n2, atol=1e-6, rtol=1e-5)
+    # the same kernels on the same records: the outputs agree bitwise
+    assert torch.equal(seg.out0, o2) and torch.equal(seg.qt, q2)
     s0 = x.state[0]
     _, ref = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
                        x.scale)
     from helpers import rel_fro
     err = rel_fro((s0 @ m1 + n1)[None].cpu(), ref.cpu())
     assert err.max().item() < 1e-2
+    # outputs from s0 by the correction equal a run from s0 to the prefill tolerance
+    ref_o = K.prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens,
+                      x.scale)[0]
+    out, end = seg.finish(s0, CP._default_affine())
+    torch.cuda.synchronize()
+    assert_prefill_close(out.cpu(), end[None].cpu(), ref_o.cpu(), ref.cpu())
 
 
-def _emulate(x, world):
+def _emulate(x, world, first_weight=1.0):
+    """cp_prefill's steps for every virtual rank in turn: rank 0 runs its
+    segment outright, the others run pass A; then each folds the maps before it
+    and finishes (output correction and end state)."""
     T = x.q.shape[0]
-    segs = CP.cp_segments(T, world)
-    maps = []
-    for lo, hi in segs:                         # pass A on every virtual rank
-        if hi > lo:
-            maps.append(CP.segment_affine(x.q[lo:hi], x.k[lo:hi], x.v[lo:hi], x.A_log,
-                                          x.a[lo:hi], x.dt_bias, x.b[lo:hi], x.scale))
-        else:
+    segs = CP.cp_segments(T, world, first_weight)
+    maps, runs = [], []
+    for r, (lo, hi) in enumerate(segs):
+        sl = lambda t: t[lo:hi].contiguous()
+        args = (sl(x.q), sl(x.k), sl(x.v))
+        gates = (x.A_log, sl(x.a), x.dt_bias, sl(x.b), x.scale)
+        if hi == lo:
             maps.append((torch.eye(128, device="cuda").expand(32, 128, 128).contiguous(),
                          torch.zeros(32, 128, 128, device="cuda")))
+            runs.append(None)
+        elif r == 0:
+            direct = CP._run_direct(None, *args, x.state[0], *gates)
+            maps.append((torch.zeros(32, 128, 128, device="cuda"), direct[1]))
+            runs.append(direct)
+        else:
+            seg = CP._KernelSegment(*args, *gates)
+            maps.append(seg.pass_a())
+            runs.append(seg)
     outs, end = [], None
-    for r, (lo, hi) in enumerate(segs):         # fold + pass B
+    for r, run in enumerate(runs):
         s_in = CP.fold_states(x.state[0], maps[:r])
-        if hi == lo:
+        if run is None:
             end = s_in
-            continue
-        o, ns = K.prefill(x.q[lo:hi], x.k[lo:hi], x.v[lo:hi], s_in[None].contiguous(), x.A_log,
-                          x.a[lo:hi], x.dt_bias, x.b[lo:hi],
-                          torch.tensor([0, hi - lo], dtype=torch.int32, device="cuda"), x.scale)
-        outs.append(o)
-        end = ns[0]
+        elif r == 0:
+            outs.append(run[0])
+            end = run[1]
+        else:
+            o, end = run.finish(s_in, CP._default_affine())
+            outs.append(o)
     return torch.cat(outs), end
 
 
-@pytest.mark.parametrize("T,world", [(4096, 2), (8192, 4), (1000, 3), (100, 3)])
-def test_cp_emulated_matches_whole_sequence(T, world):
+@pytest.mark.parametrize("T,world,w", [(4096, 2, 1.0), (8192, 4, 1.3), (1000, 3, 1.0),
+                                       (100, 3, 1.0), (20000, 2, 1.3)])
+def test_cp_emulated_matches_whole_sequence(T, world, w):
     x = W.make_prefill_inputs([T], seed=200 + world, device="cuda")
-    out, end = _emulate(x, world)
+    out, end = _emulate(x, world, w)
     torch.cuda.synchronize()
     c = {n: getattr(x, n).cpu() for n in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b",
                                           "cu_seqlens")}
