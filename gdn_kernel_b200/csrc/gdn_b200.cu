@@ -436,21 +436,38 @@ void launch_prepare(const SplitParams& sp, const CUtensorMap& tq, const CUtensor
 // ceil(n / SMs) waves of 1.2 t, so the wide form wins once 2n > SMs.  (The
 // one-sequence pieces path keeps the narrow form: its idle SMs run the prep.)
 void launch_recur(const SplitParams& sp, const CUtensorMap& tk, const CUtensorMap& tv,
-                  int64_t num_seqs, int32_t num_v_heads, cudaStream_t st, bool allow_wide = true) {
+                  int64_t num_seqs, int32_t num_v_heads, cudaStream_t st, bool allow_wide = true,
+                  bool pdl = false) {
   // (num_seqs: CTA rows of the grid; with sp.scan each row runs a window's candidates)
+  // pdl: launched with programmatic serialization after an overlapping prep, so
+  // the grid is resident when the chain before it ends (it waits for the prep
+  // inside); otherwise a plain launch.
   const bool wide = allow_wide && 2 * num_seqs * num_v_heads > static_cast<int64_t>(device_sm_count());
   const dim3 g(static_cast<unsigned>((wide ? 1 : 2) * num_v_heads), static_cast<unsigned>(num_seqs));
-  if (wide) {
-    if (sp.scan)
-      gdn_prefill_chain_kernel<128, true><<<g, kC2Threads, ChainLayout<128>::kSmem, st>>>(tk, tv, sp);
-    else
-      gdn_prefill_chain_kernel<128, false><<<g, kC2Threads, ChainLayout<128>::kSmem, st>>>(tk, tv, sp);
-  } else {
-    if (sp.scan)
-      gdn_prefill_chain_kernel<64, true><<<g, kC2Threads, ChainLayout<64>::kSmem, st>>>(tk, tv, sp);
-    else
-      gdn_prefill_chain_kernel<64, false><<<g, kC2Threads, ChainLayout<64>::kSmem, st>>>(tk, tv, sp);
-  }
+  auto go = [&](void (*kern)(const CUtensorMap, const CUtensorMap, const SplitParams),
+                uint32_t smem) {
+    if (pdl) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = g;
+      cfg.blockDim = dim3(kC2Threads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, kern, tk, tv, sp) == cudaSuccess) return;
+      (void)cudaGetLastError();   // as a plain launch below: the same results
+    }
+    kern<<<g, kC2Threads, smem, st>>>(tk, tv, sp);
+  };
+  if (wide)
+    go(sp.scan ? gdn_prefill_chain_kernel<128, true> : gdn_prefill_chain_kernel<128, false>,
+       ChainLayout<128>::kSmem);
+  else
+    go(sp.scan ? gdn_prefill_chain_kernel<64, true> : gdn_prefill_chain_kernel<64, false>,
+       ChainLayout<64>::kSmem);
 }
 
 // A whole two-stage call.  One short-grid sequence (its chain kernel fills at
@@ -505,7 +522,7 @@ void launch_two_stage(const SplitParams& sp, const CUtensorMap& tq, const CUtens
       launch_table_then_prep(piece, tq, tk, items, 2LL * sms, st);
     else
       launch_prep(piece, tq, tk, items, 2LL * (sms - chain_ctas), true, st);
-    launch_recur(piece, tk, tv, num_seqs, num_v_heads, st);
+    launch_recur(piece, tk, tv, num_seqs, num_v_heads, st, true, i > 0);
     lo = hi;
   }
 }
@@ -553,7 +570,7 @@ void launch_windows(const SplitParams& sp0, const CUtensorMap& tq, const CUtenso
     else
       launch_prep(win, tq, tk, items, free_ctas, true, st);
     if (!interleave) {
-      launch_recur(win, tk, tv, num_seqs, num_v_heads, st, false);
+      launch_recur(win, tk, tv, num_seqs, num_v_heads, st, false, i > 0);
     } else if (i == 0) {
       // every sequence gets a CTA row once (empty sequences copy their state)
       launch_recur(win, tk, tv, num_seqs, num_v_heads, st, true);

@@ -375,6 +375,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     return reinterpret_cast<float*>(smem + kP1OffGate + kGateFloats * 4 * r);
   };
 
+  // The chain grid launched after this one (one-sequence pieces) may be
+  // launched now; its CTAs wait for SMs and then for this grid's completion.
+  pdl_launch_dependents();
   if (warp == 0) {
     tmem_alloc(tmem_ptr, kP1TmCols);
     tmem_relinquish();
@@ -734,7 +737,13 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   const int head = blockIdx.x / (kHeadDim / kVS), vs = blockIdx.x % (kHeadDim / kVS);
   const int hq = head / (p.h_v / p.h_qk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  pdl_launch_dependents();   // a prep grid of the next piece may take the other SMs
+  // A chain grid launched with programmatic serialization after the prep that
+  // overlapped the chain before it is resident before that chain ends; it waits
+  // here until the prep (and so the chain before it) has completed, which
+  // precedes every read of a record or state.  Only then may the next piece's
+  // prep start, so it cannot take SMs from this grid's CTAs still arriving.
+  pdl_wait();
+  pdl_launch_dependents();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + L::kOffTmemPtr);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
