@@ -439,9 +439,10 @@ void launch_recur(const SplitParams& sp, const CUtensorMap& tk, const CUtensorMa
                   int64_t num_seqs, int32_t num_v_heads, cudaStream_t st, bool allow_wide = true,
                   bool pdl = false) {
   // (num_seqs: CTA rows of the grid; with sp.scan each row runs a window's candidates)
-  // pdl: launched with programmatic serialization after an overlapping prep, so
-  // the grid is resident when the chain before it ends (it waits for the prep
-  // inside); otherwise a plain launch.
+  // pdl: launched with programmatic serialization after the prep whose records
+  // it reads (which triggers at its start), so the grid's CTAs take SMs as the
+  // prep's CTAs, or those of the chain before, retire, and wait inside for the
+  // prep's completion; otherwise a plain launch.
   const bool wide = allow_wide && 2 * num_seqs * num_v_heads > static_cast<int64_t>(device_sm_count());
   const dim3 g(static_cast<unsigned>((wide ? 1 : 2) * num_v_heads), static_cast<unsigned>(num_seqs));
   auto go = [&](void (*kern)(const CUtensorMap, const CUtensorMap, const SplitParams),
@@ -522,6 +523,9 @@ void launch_two_stage(const SplitParams& sp, const CUtensorMap& tq, const CUtens
       launch_table_then_prep(piece, tq, tk, items, 2LL * sms, st);
     else
       launch_prep(piece, tq, tk, items, 2LL * (sms - chain_ctas), true, st);
+    // The first piece's chain is a plain launch: launched by programmatic
+    // serialization after the first prep, one sequence ran slower on B200
+    // (8,192 tokens 255 -> 270 us, 65,536 tokens 1.67 -> 1.85 ms).
     launch_recur(piece, tk, tv, num_seqs, num_v_heads, st, true, i > 0);
     lo = hi;
   }
@@ -573,10 +577,10 @@ void launch_windows(const SplitParams& sp0, const CUtensorMap& tq, const CUtenso
       launch_recur(win, tk, tv, num_seqs, num_v_heads, st, false, i > 0);
     } else if (i == 0) {
       // every sequence gets a CTA row once (empty sequences copy their state)
-      launch_recur(win, tk, tv, num_seqs, num_v_heads, st, true);
+      launch_recur(win, tk, tv, num_seqs, num_v_heads, st, true, true);
     } else {
       win.scan = 1;   // K CTA rows run the window's candidate sequences
-      launch_recur(win, tk, tv, sp.group, num_v_heads, st, true);
+      launch_recur(win, tk, tv, sp.group, num_v_heads, st, true, true);
     }
   }
 }
