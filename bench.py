@@ -505,6 +505,21 @@ def prefill_drift_and_cpu(case, lengths):
            "sample": f"the whole case ({T} tokens, {len(lengths)} sequences) through the fp32 "
                      f"chunked CPU oracle (torch, {torch.get_num_threads()} threads): "
                      f"{sec:.2f} s"}
+    # The token-by-token recurrence (the reference's own sequential form, batched
+    # over heads) on a prefix of the first sequence: its per-token cost does not
+    # depend on the position, so the prefix rate is the whole case's.
+    n = min(lengths[0], 2048)
+    st0 = None if x["state"] is None else x["state"][:1]
+    t0 = time.perf_counter()
+    O.prefill_sequential(x["q"][:n], x["k"][:n], x["v"][:n], st0, x["A_log"], x["a"][:n],
+                         x["dt_bias"], x["b"][:n], torch.tensor([0, n], dtype=torch.int32),
+                         x["scale"])
+    sec_seq = time.perf_counter() - t0
+    cpu["sequential"] = {"value": round(n / sec_seq, 1), "unit": "tokens/s",
+                         "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"the first {n} tokens of sequence 0 through the fp32 "
+                                   f"token-sequential CPU oracle (torch, "
+                                   f"{torch.get_num_threads()} threads): {sec_seq:.2f} s"}
     return drift, cpu, ro
 
 
@@ -608,6 +623,17 @@ def _max_over_ranks(ms, world):
     return float(t.item())
 
 
+def _per_rank(value, world):
+    """The value of every rank, in rank order (every rank calls this in turn)."""
+    if world == 1:
+        return [value]
+    import torch.distributed as dist
+    t = torch.tensor([float(value)], dtype=torch.float64, device="cuda")
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [float(x.item()) for x in parts]
+
+
 def run_sharded(K, rank, world, flush, hbm_peak):
     """a fixed whole-box workload partitioned by sequence
     (strong scaling): (a) decode B=1024 as contiguous batch blocks; (b) packed
@@ -620,18 +646,22 @@ def run_sharded(K, rank, world, flush, hbm_peak):
     if world > 1:
         dist.barrier()
     ts = time_decode(K, hi - lo, 20, 3, flush, seed=5000 + rank)
+    per_rank = _per_rank(statistics.median(ts) * 1e3, world)
     ms = _max_over_ranks(statistics.median(ts), world)
     step_bytes = 1024 * STATE_BYTES_PER_SEQ
     gbps = step_bytes / (ms * 1e-3) / 1e9
     res["decode_B1024"] = {"us_per_step": round(ms * 1e3, 2), "state_GBps": round(gbps, 1),
                            "per_gpu_frac_hbm": round(gbps / world / hbm_peak, 4),
                            "box_frac_hbm": round(gbps / (world * hbm_peak), 4),
-                           "batch_per_gpu": hi - lo}
+                           "batch_per_gpu": hi - lo,
+                           "per_rank_us": [round(x, 2) for x in per_rank]}
     lengths = W.varlen_lengths(64, 1024, 16384, seed=4)
     mine = [lengths[i] for i in S.prefill_shards(lengths, world)[rank]]
     if world > 1:
         dist.barrier()
     pts = time_prefill(K, mine, 3, 2, flush, seed=6000 + rank) if mine else [0.0]
+    per_rank = _per_rank(statistics.median(pts) * 1e3, world)
+    per_rank_tokens = _per_rank(sum(mine), world)
     pms = _max_over_ranks(statistics.median(pts), world)
     T = sum(lengths)
     hb = prefill_hbm_bytes(lengths, True)
@@ -639,7 +669,9 @@ def run_sharded(K, rank, world, flush, hbm_peak):
                             "tokens_per_s": round(T / (pms * 1e-3), 1),
                             "hbm_GBps": round(hb / (pms * 1e-3) / 1e9, 1),
                             "box_frac_hbm": round(hb / (pms * 1e-3) / 1e9 / (world * hbm_peak), 4),
-                            "tokens_this_rank": sum(mine)}
+                            "tokens_this_rank": sum(mine),
+                            "per_rank_us": [round(x, 1) for x in per_rank],
+                            "per_rank_tokens": [int(x) for x in per_rank_tokens]}
     # (c) one long sequence split over the ranks (context-parallel prefill; one
     # all-gather of the per-segment affine state maps per call)
     res["prefill_context_parallel"] = time_context_parallel(K, rank, world, flush, 65536)
@@ -685,9 +717,13 @@ def time_context_parallel(K, rank, world, flush, total_tokens, iters=3, warmup=1
         e1.record()
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1))
+    per_rank = _per_rank(statistics.median(ts) * 1e3, world)
+    per_rank_tokens = _per_rank(hi - lo, world)
     ms = _max_over_ranks(statistics.median(ts), world)
     del x
     return {"tokens": total_tokens, "us": round(ms * 1e3, 1),
+            "per_rank_us": [round(v, 1) for v in per_rank],
+            "per_rank_segment_tokens": [int(v) for v in per_rank_tokens],
             "tokens_per_s": round(total_tokens / (ms * 1e-3), 1),
             "segment_tokens_this_rank": hi - lo,
             "method": "single call (one sequence in overlapping pieces)" if world == 1 else
