@@ -532,10 +532,11 @@ void launch_two_stage(const SplitParams& sp, const CUtensorMap& tq, const CUtens
 }
 
 // A two-stage call whose records do not all fit the record rows of the
-// workspace (a ring of sp.ring_rows rows): consecutive windows of W =
-// ring_rows / 2 table chunks, the records of chunk g in row g % ring_rows, so
-// that a window's records fill one half of the ring while the chain of the
-// window before it reads the other half.  The host knows only an upper bound
+// workspace (a ring of sp.ring_rows rows): consecutive windows of W table
+// chunks, the records of chunk g in row g % ring_rows.  With one sequence W =
+// ring_rows / 2, so that a window's records fill one half of the ring while
+// the chain of the window before it reads the other half; with several, W =
+// ring_rows (below).  The host knows only an upper bound
 // of the chunk count (ceil(T / 64) + N); windows past the table's real end
 // find no items and no chunks.
 //  * One sequence: as in the one-sequence pieces, the prep of window i + 1 is
@@ -554,8 +555,12 @@ void launch_windows(const SplitParams& sp0, const CUtensorMap& tq, const CUtenso
                     int32_t num_v_heads, cudaStream_t st) {
   const int sms = device_sm_count();
   SplitParams sp = sp0;
-  const long long window = sp.ring_rows / 2;
   const bool interleave = num_seqs > 1;
+  // One sequence: half the ring per window, so that a window's prep fills one
+  // half while the chain of the window before reads the other.  Several
+  // sequences: a window's prep follows the previous window's chain (a plain
+  // launch), so each window takes the whole ring.
+  const long long window = interleave ? sp.ring_rows : sp.ring_rows / 2;
   if (interleave) {
     sp.group = std::max(1, std::min<int>(kMaxGroup, sms / std::max(1, num_v_heads)));
     sp.block = static_cast<int>(std::max<long long>(1, window / sp.group));
@@ -579,8 +584,14 @@ void launch_windows(const SplitParams& sp0, const CUtensorMap& tq, const CUtenso
       // every sequence gets a CTA row once (empty sequences copy their state)
       launch_recur(win, tk, tv, num_seqs, num_v_heads, st, true, true);
     } else {
-      win.scan = 1;   // K CTA rows run the window's candidate sequences
-      launch_recur(win, tk, tv, sp.group, num_v_heads, st, true, true);
+      // CTA rows walk the window's candidate sequences: about as many rows as
+      // a window holds sequences of the mean length, plus a partial group at
+      // either end (more candidates loop over the rows).
+      win.scan = 1;
+      const long long mean = std::max<long long>(1, (L.max_chunks - num_seqs) / num_seqs);
+      const long long rows =
+          std::min<long long>(num_seqs, std::max<long long>(sp.group, window / mean + 2 * sp.group));
+      launch_recur(win, tk, tv, rows, num_v_heads, st, true, true);
     }
   }
 }

@@ -90,8 +90,11 @@ int gdn_b200_decode_pool(const void* q, const void* k, const void* v,
                          int64_t pool_size, int32_t num_qk_heads, int32_t num_v_heads,
                          int32_t head_dim, void* stream);
 
-/* Capacity (bytes) of the record ring that gdn_b200_prefill works in. */
-#define GDN_B200_PREFILL_RING_BYTES (128ull << 20)
+/* Capacity (bytes) of the record ring that gdn_b200_prefill works in: 1 GiB,
+ * the records of about 42,000 tokens of one sequence at qk16_v32 (0.6 % of a
+ * B200's HBM).  (The host side of a device array of 2 GiB or more does not
+ * link with the default small code model.) */
+#define GDN_B200_PREFILL_RING_BYTES (1024ull << 20)
 
 /*
  * Chunked (C=64) prefill over `num_seqs` packed variable-length sequences.

@@ -258,11 +258,15 @@ def test_unordered_cu_seqlens_flagged_and_bounded():
     assert torch.count_nonzero(ns2[1]) == 0
 
 
+# The 1 GiB ring holds 668 record rows at qk16_v32: one sequence runs in
+# windows of 334 chunks, several sequences in windows of 668.
 RING_CASES = [
     ([150, 0, 64, 33], True, False),       # records fit the ring: one window
-    ([8192], False, False),                # one sequence over four ring windows
-    ([12000], True, True),                 # in place, six windows
-    ([3000, 0, 5000, 4000, 1], True, False),   # windows that span sequence boundaries
+    ([8192], False, False),                # fits: the one-sequence pieces path
+    ([50000], False, False),               # one sequence over three ring windows
+    ([60000], True, True),                 # in place, three windows
+    ([20000, 0, 15000, 12000, 1], True, False),   # windows that span sequence boundaries
+    ([9000] * 6 + [300, 0, 2], True, False),      # three interleaved groups, two windows
 ]
 
 
@@ -287,9 +291,9 @@ def test_ring_path_bitwise_equal_to_workspace(lengths, with_state, in_place):
 
 
 def test_ring_path_matches_oracle_over_windows():
-    """Five ring windows (a 6,000-token sequence after a short one) against the
-    fp32 oracle."""
-    lengths = [100, 6000]
+    """Two ring windows (a 44,000-token sequence after a short one: 692 chunks
+    against 668 record rows) against the fp32 oracle."""
+    lengths = [100, 44000]
     x = W.make_prefill_inputs(lengths, seed=52)
     out, ns = _run(x, "ring")
     ro, rs = _oracle(x)
@@ -322,7 +326,7 @@ def test_ring_path_interleaved_groups():
     interleaves groups of sequences so that each ring window holds a run of
     chunks of every group member (group and round sizes from the window size).
     Bit-identical to the workspace path, and within tolerance of the oracle."""
-    lengths = [700, 3000, 1, 2500, 4100, 0, 1800, 640, 5000]
+    lengths = [2100, 9000, 1, 7500, 12300, 0, 5400, 1920, 15000]   # 840 chunks, 668 rows
     x = W.make_prefill_inputs(lengths, seed=55)
     o1, s1 = _run(x, "ring")
     o2, s2 = _run(x, "split")
