@@ -63,6 +63,7 @@ _SIGNATURES = {
                                               ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_uint64,
                                               _P]),
     "gdn_b200_state_affine": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64, _P]),
+    "gdn_b200_current_device": (ctypes.c_int32, []),
     "gdn_b200_device_status": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32),
                                               ctypes.c_int32]),
     "gdn_b200_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _P]),

@@ -998,4 +998,13 @@ extern "C" int gdn_b200_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
   return GDN_B200_OK;
 }
 
-extern "C" int32_t gdn_b200_abi_version(void) { return 102; }
+extern "C" int32_t gdn_b200_abi_version(void) { return 103; }
+
+extern "C" int32_t gdn_b200_current_device(void) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -1;
+  }
+  return dev;
+}

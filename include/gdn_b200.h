@@ -274,6 +274,16 @@ int gdn_b200_selftest_prefill_abort(uint64_t limit_ns, const void* k, const void
                                     int32_t num_v_heads, int32_t head_dim, const void* workspace,
                                     uint64_t workspace_bytes, void* stream);
 
+/*
+ * The device this library launches on from the calling thread: the device of
+ * the thread's current CUDA context (set by cudaSetDevice in any runtime of the
+ * process, e.g. torch.cuda.device), or -1 if none can be read.  Every entry
+ * point launches on, and sets up, this device, so a caller whose tensors live
+ * on another device makes that device current first.  No counterpart in the
+ * reference.
+ */
+int32_t gdn_b200_current_device(void);
+
 /* Message of the last failing call on this thread ("" if none). */
 const char* gdn_b200_last_error(void);
 

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for name in _declared():
         assert hasattr(lib, name), name
     assert set(_declared()) == set(_lib._SIGNATURES), "ctypes table out of sync with the header"
-    assert lib.gdn_b200_abi_version() == 102
+    assert lib.gdn_b200_abi_version() == 103
 
 
 def _decode_call(lib, **kw):

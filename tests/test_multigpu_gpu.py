@@ -65,3 +65,50 @@ def test_multi_gpu_context_parallel_prefill(world):
     ro, rs = O.prefill_chunked(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b,
                                x.cu_seqlens, x.scale)
     assert_prefill_close(out, end[None], ro, rs)
+
+
+def test_calls_on_another_device_make_it_current():
+    """Tensors on cuda:1 while device 0 is current: the wrappers and the TVM-FFI
+    exports make the tensors' device current for the call (the library launches
+    on the current device) and restore device 0.  First the library must see
+    torch's device switch at all (it links its own CUDA runtime, which follows
+    the thread's current context); only then are kernels launched, and their
+    results must equal the same calls made with device 1 current."""
+    _need(2)
+    from gdn_kernel_b200 import _lib
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    assert lib.gdn_b200_current_device() == 0
+    with torch.cuda.device(1):
+        assert lib.gdn_b200_current_device() == 1
+    assert lib.gdn_b200_current_device() == 0
+
+    dev = torch.device("cuda", 1)
+    xd = W.make_decode_inputs(4, seed=3, device=dev)
+    xp = W.make_prefill_inputs([300, 0, 2000], seed=4, device=dev)
+
+    def run():
+        st = xd.state.clone()
+        out = torch.empty(4, 1, 32, 128, dtype=torch.bfloat16, device=dev)
+        K.gdn_decode(xd.q, xd.k, xd.v, st, xd.A_log, xd.a, xd.dt_bias, xd.b, xd.scale, out, st)
+        res = [out, st]
+        for path in ("split", "ring"):
+            res += list(K.prefill(xp.q, xp.k, xp.v, xp.state, xp.A_log, xp.a, xp.dt_bias, xp.b,
+                                  xp.cu_seqlens, xp.scale, path=path))
+        tvm_dec, tvm_pre = K.load_tvm_kernel("decode"), K.load_tvm_kernel("prefill")
+        o2, s2 = torch.empty_like(out), xd.state.clone()
+        tvm_dec(xd.q, xd.k, xd.v, s2, xd.A_log, xd.a, xd.dt_bias, xd.b, xd.scale, o2, s2)
+        o3 = torch.empty(2300, 32, 128, dtype=torch.bfloat16, device=dev)
+        s3 = torch.empty_like(xp.state)
+        tvm_pre(xp.q, xp.k, xp.v, xp.state, xp.A_log, xp.a, xp.dt_bias, xp.b, xp.cu_seqlens,
+                xp.scale, o3, s3)
+        torch.cuda.synchronize(dev)
+        return res + [o2, s2, o3, s3]
+
+    got = run()                      # device 0 current
+    assert torch.cuda.current_device() == 0 and lib.gdn_b200_current_device() == 0
+    assert _lib.device_status(1) == 0 and _lib.device_status(0) == 0
+    with torch.cuda.device(1):
+        ref = run()
+    for a, b in zip(got, ref):
+        assert a.device == dev and torch.equal(a, b)
