@@ -489,8 +489,10 @@ __device__ __forceinline__ void qprime_row(uint8_t* tile, int c, float e, const 
 // F[j] = e^{gamma_{j|7} - gamma_j} (the decay from j to the end of its
 // 8-position sub-block, used by decay_row).
 // Positions past the sequence end get log g = 0 and beta = 0.
+// The inputs stay bf16 until gate_finish: a conversion here would make the
+// warp wait for the loads where they are issued.
 struct GateIn {
-  float a[2], b[2];
+  __nv_bfloat16 a[2], b[2];
   bool valid[2];
 };
 
@@ -503,10 +505,10 @@ __device__ __forceinline__ GateIn gate_inputs(const PrefillParams& p, long long 
     g.valid[e] = pos < clen;
     if (g.valid[e]) {
       const size_t t = static_cast<size_t>(cstart + pos) * p.h_v + head;
-      g.a[e] = __bfloat162float(p.a[t]);
-      g.b[e] = __bfloat162float(p.b[t]);
+      g.a[e] = p.a[t];
+      g.b[e] = p.b[t];
     } else {
-      g.a[e] = g.b[e] = 0.f;
+      g.a[e] = g.b[e] = __float2bfloat16(0.f);
     }
   }
   return g;
@@ -517,8 +519,8 @@ __device__ __forceinline__ void gate_finish(const GateIn& g, float A_neg, float 
   float lg[2], bt[2];
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
-    lg[e] = g.valid[e] ? A_neg * softplus20p(g.a[e] + dtb) : 0.f;
-    bt[e] = g.valid[e] ? 1.0f / (1.0f + expf(-g.b[e])) : 0.f;
+    lg[e] = g.valid[e] ? A_neg * softplus20p(__bfloat162float(g.a[e]) + dtb) : 0.f;
+    bt[e] = g.valid[e] ? 1.0f / (1.0f + expf(-__bfloat162float(g.b[e]))) : 0.f;
   }
   float x = lg[0] + lg[1];
 #pragma unroll

@@ -537,6 +537,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     tc_fence_after();
     pa_epilogue(tmem + tm_lane + kP1TmQK, row, half, quad, clen, gam, bet, gam + 192, tpzt + 8192,
                 AF);
+    // The next item's gates (loaded at the top of this item) into the other
+    // buffer, by warp 1, which finishes its share of the epilogue early.  That
+    // buffer's previous contents (item j - 1's gamma) left with item j - 1's
+    // records, whose read-out the store thread waited for before the barrier
+    // above.  At the end of the item this made warp 1 the last warp into the
+    // next item's first barrier.
+    if (has_nxt) finish_gates(gi, r ^ 1);
     tc_fence_before();
     __syncthreads();
     solve_unit_lower(AF, TF, XS, tpzt, bet, eg, tid);
@@ -606,9 +613,6 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
         qprime_row(tile, row - 64, eg[row - 64], rr);
       }
     }
-    // The next item's gates (its loads have landed by now) into the other buffer;
-    // that buffer's previous contents (item j - 1's gamma) were drained above.
-    if (has_nxt) finish_gates(gi, r ^ 1);
     fence_proxy_async_smem();
     tc_fence_before();
     // Only the store thread's warp waits for the finished tiles; the others
@@ -618,7 +622,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 2)
     // Tile images out by bulk copies ([Q' ; -W], P', T_b, gamma); drained by
     // the next item (or the end of the kernel) before their sources change.
     // A thread of the last warp issues them, off warp 0's path to the next
-    // item's first product.
+    // item's first product.  (Writing the [Q' ; -W] rows straight from
+    // registers instead, one row per thread, was slower on B200.)
     if (tid == kP1StoreTid) {
       uint8_t* rec = record_at(sp, gc, head);
       bulk_store(rec + kRecOffQW, qkw, 32768);
