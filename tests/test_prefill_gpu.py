@@ -334,3 +334,41 @@ def test_ring_path_interleaved_groups():
     assert torch.equal(s1, s2)
     ro, rs = _oracle(x)
     assert_prefill_close(o1, s1, ro, rs, lengths)
+
+
+def test_configs4_scale_ring_equals_workspace_and_oracle_on_samples():
+    """The 64 sequences of U[1024, 16384] tokens (about 552K, BASELINE
+    configs[4]) in one packed call: the ring path (windows over the 1 GiB
+    ring) equals the workspace path bit for bit, and two of the packed
+    sequences equal the fp32 oracle run on those sequences alone (sequences
+    are independent), to the prefill tolerance."""
+    lengths = W.varlen_lengths(64, 1024, 16384, seed=4)
+    x = W.make_prefill_inputs(lengths, seed=9, device="cuda")
+    args = (x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale)
+    o1, s1 = K.prefill(*args, path="split")
+    o2, s2 = K.prefill(*args, path="ring")
+    torch.cuda.synchronize()
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    cu = x.cu_seqlens.cpu().tolist()
+    for n in (0, 37):
+        lo, hi = cu[n], cu[n + 1]
+        sl = lambda t: t[lo:hi].cpu()
+        ro, rs = O.prefill_chunked(sl(x.q), sl(x.k), sl(x.v), x.state[n:n + 1].cpu(),
+                                   x.A_log.cpu(), sl(x.a), x.dt_bias.cpu(), sl(x.b),
+                                   torch.tensor([0, hi - lo], dtype=torch.int32), x.scale)
+        assert_prefill_close(o1[lo:hi].cpu(), s1[n:n + 1].cpu(), ro, rs)
+
+
+def test_long_sequence_ring_windows_equal_workspace():
+    """One 65,536-token sequence (1,025 chunks over 334-chunk ring windows)
+    equals the workspace path (eight overlapping pieces) bit for bit, in
+    place, from a random initial state."""
+    x = W.make_prefill_inputs([65536], seed=10, device="cuda", with_state=True)
+    args = (x.q, x.k, x.v, x.A_log, x.a, x.dt_bias, x.b, x.cu_seqlens, x.scale)
+    st1, st2 = x.state.clone(), x.state.clone()
+    o1, s1 = K.prefill(x.q, x.k, x.v, st1, *args[3:], in_place=True, path="split")
+    o2, s2 = K.prefill(x.q, x.k, x.v, st2, *args[3:], in_place=True, path="ring")
+    torch.cuda.synchronize()
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
