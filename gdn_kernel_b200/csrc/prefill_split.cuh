@@ -237,11 +237,32 @@ __global__ void __launch_bounds__(kTableThreads) gdn_chunk_table_kernel(SplitPar
     sp.header[0] = total;
   }
   __syncthreads();   // pass 2 reads the chunk counts of a sequence's whole group
+  if (!overflow && sp.group <= 1) {
+    // Sequence-major table: every thread fills table positions directly (the
+    // owner of position c is the last sequence whose first chunk is <= c), so a
+    // long sequence's entries are not written by one thread.
+    for (int c = tid; c < total; c += kTableThreads) {
+      int lo = 0, hi = sp.num_seqs - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sp.seq_off[mid] <= c) lo = mid;
+        else hi = mid - 1;
+      }
+      long long s0, s1;
+      seq_range(p, lo, s0, s1);
+      ChunkInfo e;
+      e.seq = lo;
+      e.cstart = s0 + static_cast<long long>(c - sp.seq_off[lo]) * kChunk;
+      e.clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - e.cstart));
+      sp.table[c] = e;
+    }
+  }
   for (int i = tid; i < sp.num_seqs; i += kTableThreads) {
     if (overflow) {   // overlapping sequences: all are treated as empty
       sp.seq_off[i] = 0;
       continue;
     }
+    if (sp.group <= 1) continue;   // written above
     long long s0, s1;
     seq_range(p, i, s0, s1);
     const GroupView g = group_view(sp, i);
