@@ -686,7 +686,7 @@ def time_context_parallel(K, rank, world, flush, total_tokens, iters=3, warmup=1
     import torch.distributed as dist
 
     x = W.make_prefill_inputs([total_tokens], seed=6100, device="cuda")
-    lo, hi = CP.cp_segments(total_tokens, world, CP.FIRST_SEGMENT_WEIGHT)[rank]
+    lo, hi = CP.cp_segments(total_tokens, world, CP.first_segment_weight(world))[rank]
     if world == 1:
         out = torch.empty(total_tokens, H_V, D, dtype=torch.bfloat16, device="cuda")
         ns = torch.empty(1, H_V, D, D, dtype=torch.float32, device="cuda")

@@ -32,7 +32,7 @@ per-head sequential depth drops from T/64 chunks to about T/(64 G).  A rank
 other than 0 spends more per token than rank 0 (the records are prepared
 before its chain starts, two recurrences share its SMs, and the correction
 reads its outputs again), so ``cp_segments`` can give rank 0 a larger share
-(``FIRST_SEGMENT_WEIGHT``).  The reference is single-GPU (its harness requests
+(``first_segment_weight``).  The reference is single-GPU (its harness requests
 one B200, ref scripts/run_modal.py:36); this is the split its recurrence
 admits.
 
@@ -53,8 +53,16 @@ CHUNK = 64
 
 # Per-token cost of a rank other than 0 (prepare, then two concurrent
 # recurrences, then the output correction) over that of rank 0's direct
-# one-sequence prefill, measured on B200 at qk16_v32.
+# one-sequence prefill, measured on B200 at qk16_v32 for 65,536 tokens: 1.3 was
+# the best of a sweep at 2 ranks; at 4 ranks (1.3 given) rank 0 ran 38.9 us per
+# 1K tokens and the others 58.4, a ratio of 1.5 (their fixed costs, the
+# gather, fold and correction, weigh more on shorter segments).
 FIRST_SEGMENT_WEIGHT = 1.3
+
+
+def first_segment_weight(world: int) -> float:
+    """The ``first_weight`` of ``cp_segments`` for ``world`` ranks."""
+    return 1.0 if world <= 1 else (FIRST_SEGMENT_WEIGHT if world == 2 else 1.5)
 
 
 def cp_segments(total_tokens: int, world: int, first_weight: float = 1.0

@@ -37,6 +37,14 @@ def test_weighted_segments(T, world, w):
         assert abs(chunks[0] - nch * w / (w + world - 1)) <= 1
 
 
+def test_first_segment_weight_by_world():
+    assert CP.first_segment_weight(1) == 1.0
+    assert CP.first_segment_weight(2) == CP.FIRST_SEGMENT_WEIGHT
+    assert CP.first_segment_weight(8) == 1.5
+    segs = CP.cp_segments(65536, 4, CP.first_segment_weight(4))
+    assert segs[0] == (0, 21824) and all(hi - lo in (14592, 14528) for lo, hi in segs[1:])
+
+
 def test_outputs_are_affine_in_the_initial_state():
     """Pass A's two output sets give the outputs of a run from any initial
     state: O_0 + S_0 Q~ per head (oracle, fp32 runs, bf16 outputs)."""
