@@ -33,6 +33,8 @@ def test_prefill_shards_partition_and_balance():
         # LPT bound: max load <= 4/3 of the optimum; the optimum >= mean and >= the largest job
         lower = max(sum(cost) / world, max(cost))
         assert max(loads) <= 4 / 3 * lower + 1
+        for sh_r in sh:   # each rank packs its sequences longest first
+            assert [cost[i] for i in sh_r] == sorted((cost[i] for i in sh_r), reverse=True)
 
 
 def test_pack_and_scatter_roundtrip():
