@@ -358,6 +358,7 @@ SplitParams split_params(const PrefillParams& p, void* workspace, const SplitLay
   sp.zero_v = zero_v;
   sp.header = reinterpret_cast<int*>(ws + L.off_header);
   sp.seq_off = reinterpret_cast<int*>(ws + L.off_seq);
+  sp.order = reinterpret_cast<int*>(ws + L.off_order);
   sp.table = reinterpret_cast<ChunkInfo*>(ws + L.off_table);
   sp.records = ws + L.off_rec;
   sp.num_seqs = static_cast<int>(num_seqs);

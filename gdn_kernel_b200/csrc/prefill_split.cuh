@@ -50,7 +50,7 @@ constexpr uint32_t kRecOffGam = 49152;     // gamma[64], 256 B
 constexpr uint32_t kRecBytes = 50176;      // 49 KiB (keeps records 1 KiB aligned)
 
 struct SplitLayout {
-  size_t off_header, off_seq, off_table, off_win, off_rec, total;
+  size_t off_header, off_seq, off_order, off_table, off_win, off_rec, total;
   long long max_chunks;
 };
 
@@ -65,7 +65,8 @@ __host__ __device__ inline SplitLayout split_layout(long long num_seqs, long lon
   auto up = [](size_t x, size_t a) { return (x + a - 1) / a * a; };
   L.off_header = 0;
   L.off_seq = 256;
-  L.off_table = up(L.off_seq + static_cast<size_t>(num_seqs + 1) * 4, 1024);
+  L.off_order = up(L.off_seq + static_cast<size_t>(num_seqs + 1) * 4, 256);
+  L.off_table = up(L.off_order + static_cast<size_t>(num_seqs) * 4, 1024);
   L.off_win = up(L.off_table + static_cast<size_t>(L.max_chunks) * sizeof(ChunkInfo), 256);
   L.off_rec = up(L.off_win + (windows ? static_cast<size_t>(L.max_chunks) * 2 * sizeof(int) : 0),
                  1024);
@@ -79,6 +80,7 @@ struct SplitParams {
   int zero_v;             // chain kernel: V is all zero (no V tiles, no M1); out may be null
   int* header;            // [0] = total chunks
   int* seq_off;           // [N + 1] first chunk of each sequence
+  int* order;             // [N] sequence of each chain CTA row (grid row y runs order[y])
   ChunkInfo* table;       // [max_chunks]
   uint8_t* records;       // [ring_rows][H_v] x kRecBytes
   int num_seqs;
@@ -167,6 +169,7 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 // ---------------------------------------------------------------- chunk table
 constexpr int kTableThreads = 1024;
+constexpr int kOrderMax = 512;   // longest-first chain rows for at most this many sequences
 
 // Token range [s0, s1) of sequence i, or an empty range (and the bad-seqlens
 // status bit) when the pair is outside 0 <= s0 <= s1 <= total_tokens.
@@ -277,6 +280,28 @@ __global__ void __launch_bounds__(kTableThreads) gdn_chunk_table_kernel(SplitPar
         c.clen = static_cast<int>(min(static_cast<long long>(kChunk), s1 - c.cstart));
         sp.table[pos + (k - k0)] = c;
       }
+    }
+  }
+  // The chain kernel's CTA rows: up to kOrderMax sequences of a sequence-major
+  // table longest first (ties: lower index), so that its first wave takes the
+  // long chains and the short ones fill in behind them; otherwise in index
+  // order.  Rank by counting, on the chunk counts staged in shared memory.
+  {
+    __shared__ int counts[kOrderMax];
+    const bool sort = !overflow && sp.group <= 1 && sp.num_seqs > 1 && sp.num_seqs <= kOrderMax;
+    if (sort) {
+      for (int i = tid; i < sp.num_seqs; i += kTableThreads)
+        counts[i] = sp.seq_off[i + 1] - sp.seq_off[i];
+      __syncthreads();
+    }
+    for (int i = tid; i < sp.num_seqs; i += kTableThreads) {
+      int rank = i;
+      if (sort) {
+        const int ni = counts[i];
+        rank = 0;
+        for (int j = 0; j < sp.num_seqs; ++j) rank += counts[j] > ni || (counts[j] == ni && j < i);
+      }
+      sp.order[rank] = i;
     }
   }
   // Windows of an interleaved table: the sequences of the groups that
@@ -768,6 +793,10 @@ __global__ void __launch_bounds__(kC2Threads, 1)
   // here until the prep (and so the chain before it) has completed, which
   // precedes every read of a record or state.  Only then may the next piece's
   // prep start, so it cannot take SMs from this grid's CTAs still arriving.
+  // This CTA row's sequence (several sequences: longest first, from the
+  // chunk-table kernel, which completed before any prep or chain of the call
+  // started, so the load may precede the wait below).
+  const int row_seq = !kScan && sp.num_seqs > 1 ? sp.order[blockIdx.y] : static_cast<int>(blockIdx.y);
   pdl_wait();
   pdl_launch_dependents();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
@@ -1153,7 +1182,7 @@ __global__ void __launch_bounds__(kC2Threads, 1)
          seq += static_cast<int>(gridDim.y))
       if (!run_sequence(seq)) break;
   } else {
-    run_sequence(static_cast<int>(blockIdx.y));
+    run_sequence(row_seq);
   }
   if (have_tmem) {
     tc_fence_before();
