@@ -337,8 +337,8 @@ def test_ring_path_interleaved_groups():
 
 
 def test_configs4_scale_ring_equals_workspace_and_oracle_on_samples():
-    """The 64 sequences of U[1024, 16384] tokens (about 552K, BASELINE
-    configs[4]) in one packed call: the ring path (windows over the 1 GiB
+    """64 sequences of U[1024, 16384] tokens (about 552K, the multi-GPU
+    benchmark's batch) in one packed call: the ring path (windows over the 1 GiB
     ring) equals the workspace path bit for bit, and two of the packed
     sequences equal the fp32 oracle run on those sequences alone (sequences
     are independent), to the prefill tolerance."""
