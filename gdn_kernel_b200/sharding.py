@@ -56,8 +56,8 @@ def prefill_shards(lengths: Sequence[int], world: int) -> List[List[int]]:
     kernel's first wave of CTAs takes the longest sequences, so the short ones
     fill in behind them.  On B200, for 64 sequences of 1,024-16,384 tokens over 8
     ranks, that cut the slowest rank from 1.69 to 1.50 ms (index order gave ranks
-    1.50-1.69 ms).  The
-    outputs go back by token and sequence index (scatter_prefill_outputs)."""
+    1.50-1.69 ms).  The outputs go back by token and sequence index
+    (scatter_prefill_outputs)."""
     if world <= 0:
         raise ValueError("world must be positive")
     cost = [max(1, math.ceil(int(L) / CHUNK)) if int(L) > 0 else 0 for L in lengths]
