@@ -563,7 +563,14 @@ void launch_windows(const SplitParams& sp0, const CUtensorMap& tq, const CUtenso
   // launch), so each window takes the whole ring.
   const long long window = interleave ? sp.ring_rows : sp.ring_rows / 2;
   if (interleave) {
-    sp.group = std::max(1, std::min<int>(kMaxGroup, sms / std::max(1, num_v_heads)));
+    // Groups of K sequences (K H_v chain CTAs fill the SMs once) are interleaved
+    // only when a window cannot hold K sequences of the mean length; otherwise
+    // the table stays sequence-major (K = 1): each window then holds whole
+    // sequences, which the chain runs side by side (varlen16 through the ring
+    // 1.67 -> 1.58 ms on B200), and only a sequence at a window's edge is split.
+    const int kfill = std::max(1, std::min<int>(kMaxGroup, sms / std::max(1, num_v_heads)));
+    const long long mean = std::max<long long>(1, (L.max_chunks - num_seqs) / num_seqs);
+    sp.group = mean * kfill > window ? kfill : 1;
     sp.block = static_cast<int>(std::max<long long>(1, window / sp.group));
     sp.window = static_cast<int>(window);
   }

@@ -266,7 +266,8 @@ RING_CASES = [
     ([50000], False, False),               # one sequence over three ring windows
     ([60000], True, True),                 # in place, three windows
     ([20000, 0, 15000, 12000, 1], True, False),   # windows that span sequence boundaries
-    ([9000] * 6 + [300, 0, 2], True, False),      # three interleaved groups, two windows
+    ([9000] * 6 + [300, 0, 2], True, False),      # sequence-major windows (short sequences)
+    ([50000, 45000, 1000], True, False),          # long sequences: one interleaved group
 ]
 
 
@@ -321,13 +322,28 @@ def test_ring_path_calls_on_two_streams():
         assert torch.equal(s, rs)
 
 
-def test_ring_path_interleaved_groups():
-    """Several sequences whose records overflow the ring: the chunk table
-    interleaves groups of sequences so that each ring window holds a run of
-    chunks of every group member (group and round sizes from the window size).
-    Bit-identical to the workspace path, and within tolerance of the oracle."""
+def test_ring_path_sequence_major_windows():
+    """Several sequences whose records overflow the ring but are short next to a
+    window: the table stays sequence-major and each window holds whole
+    sequences (one split at each window edge).  Bit-identical to the workspace
+    path, and within tolerance of the oracle."""
     lengths = [2100, 9000, 1, 7500, 12300, 0, 5400, 1920, 15000]   # 840 chunks, 668 rows
     x = W.make_prefill_inputs(lengths, seed=55)
+    o1, s1 = _run(x, "ring")
+    o2, s2 = _run(x, "split")
+    assert torch.equal(o1, o2)
+    assert torch.equal(s1, s2)
+    ro, rs = _oracle(x)
+    assert_prefill_close(o1, s1, ro, rs, lengths)
+
+
+def test_ring_path_interleaved_groups():
+    """Sequences long next to a window (17-30K tokens, 1,314 chunks
+    against 668 record rows): the chunk table interleaves them in rounds, so
+    that each ring window holds a run of chunks of every member.
+    Bit-identical to the workspace path, and within tolerance of the oracle."""
+    lengths = [30000, 29000, 8000, 0, 17000]
+    x = W.make_prefill_inputs(lengths, seed=56)
     o1, s1 = _run(x, "ring")
     o2, s2 = _run(x, "split")
     assert torch.equal(o1, o2)
