@@ -1177,10 +1177,22 @@ __global__ void __launch_bounds__(kC2Threads, 1)
 
   if constexpr (kScan) {
     const int w = sp.c_lo / sp.window;
-    const int s_end = sp.win_seq[2 * w + 1];
-    for (int seq = sp.win_seq[2 * w] + static_cast<int>(blockIdx.y); seq < s_end;
-         seq += static_cast<int>(gridDim.y))
-      if (!run_sequence(seq)) break;
+    const int s_lo = sp.win_seq[2 * w], s_end = sp.win_seq[2 * w + 1];
+    if (sp.group <= 1 && sp.num_seqs > 1 && sp.num_seqs <= kOrderMax) {
+      // the window's candidates in the longest-first order of the chunk-table
+      // kernel: the rows' first sequences are the window's long ones
+      int k = 0;
+      for (int r = 0; r < sp.num_seqs; ++r) {
+        const int seq = sp.order[r];
+        if (seq < s_lo || seq >= s_end) continue;
+        if (k++ % static_cast<int>(gridDim.y) != static_cast<int>(blockIdx.y)) continue;
+        if (!run_sequence(seq)) break;
+      }
+    } else {
+      for (int seq = s_lo + static_cast<int>(blockIdx.y); seq < s_end;
+           seq += static_cast<int>(gridDim.y))
+        if (!run_sequence(seq)) break;
+    }
   } else {
     run_sequence(row_seq);
   }
