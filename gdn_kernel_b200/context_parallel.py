@@ -55,14 +55,19 @@ CHUNK = 64
 # recurrences, then the output correction) over that of rank 0's direct
 # one-sequence prefill, measured on B200 at qk16_v32 for 65,536 tokens: 1.3 was
 # the best of a sweep at 2 ranks; at 4 ranks (1.3 given) rank 0 ran 38.9 us per
-# 1K tokens and the others 58.4, a ratio of 1.5 (their fixed costs, the
-# gather, fold and correction, weigh more on shorter segments).
+# 1K tokens and the others 58.4, a ratio of 1.5; at 8 ranks (1.5 given) 50.8
+# against about 91, a ratio of 1.8.  The fixed costs of the others (gather,
+# fold, correction) weigh more on shorter segments.
 FIRST_SEGMENT_WEIGHT = 1.3
 
 
 def first_segment_weight(world: int) -> float:
     """The ``first_weight`` of ``cp_segments`` for ``world`` ranks."""
-    return 1.0 if world <= 1 else (FIRST_SEGMENT_WEIGHT if world == 2 else 1.5)
+    if world <= 1:
+        return 1.0
+    if world == 2:
+        return FIRST_SEGMENT_WEIGHT
+    return 1.5 if world <= 4 else 1.8
 
 
 def cp_segments(total_tokens: int, world: int, first_weight: float = 1.0

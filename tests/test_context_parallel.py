@@ -40,7 +40,7 @@ def test_weighted_segments(T, world, w):
 def test_first_segment_weight_by_world():
     assert CP.first_segment_weight(1) == 1.0
     assert CP.first_segment_weight(2) == CP.FIRST_SEGMENT_WEIGHT
-    assert CP.first_segment_weight(8) == 1.5
+    assert CP.first_segment_weight(4) == 1.5 and CP.first_segment_weight(8) == 1.8
     segs = CP.cp_segments(65536, 4, CP.first_segment_weight(4))
     assert segs[0] == (0, 21824) and all(hi - lo in (14592, 14528) for lo, hi in segs[1:])
 
