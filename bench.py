@@ -566,7 +566,9 @@ def flashinfer_prefill(case, lengths, iters, warmup, flush):
             e1.record()
         torch.cuda.synchronize()
     except Exception as e:  # noqa: BLE001
-        return {"unavailable": f"flashinfer run failed: {e!r}"[:300]}
+        return {"unavailable": (f"flashinfer routes to this kernel only for torch builds with "
+                                f"CUDA >= 13 (this one: {torch.version.cuda}); called directly "
+                                f"here it fails: {e!r}")[:400]}
     ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
     return {"us": round(ms * 1e3, 1), "tokens_per_s": round(T / (ms * 1e-3), 1),
             "first_call_s": round(first_s, 1), "out": out.cpu(), "new_state": ost.cpu(),
