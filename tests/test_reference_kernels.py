@@ -68,3 +68,57 @@ def test_reference_prefill_kernel_matches_oracle_and_ours():
                        x.scale)
     torch.cuda.synchronize()
     assert_prefill_close(mo.cpu(), ms.cpu(), out.cpu(), ns.cpu(), lengths)
+
+
+def _device_us(fn, iters, warmup=1):
+    """Median device time (us) of fn() over `iters` calls, L2 evicted before each."""
+    import statistics
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    for _ in range(warmup):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(iters)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        fn()
+        e1.record()
+    torch.cuda.synchronize()
+    return statistics.median(e0.elapsed_time(e1) for e0, e1 in ev) * 1e3
+
+
+def test_faster_than_reference_kernels_on_their_layout():
+    """The reference's own CUDA kernels against this package's, on the same B200,
+    at the reference's hard-coded qk4_v8 layout and the headline shapes: decode
+    at B=64 and prefill of one 8,192-token sequence (median device time, L2
+    evicted between calls).  This package must be faster by a clear margin
+    (measured: decode about 3.5x, prefill about 250x)."""
+    ref_dec = _ref_kernel("ref_decode.so")
+    ref_pre = _ref_kernel("ref_prefill.so")
+    x = W.make_decode_inputs(64, seed=1, h_qk=4, h_v=8, device="cuda")
+    out = torch.empty(64, 1, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(64, 8, 128, 128, dtype=torch.float32, device="cuda")
+    t_ref = _device_us(lambda: ref_dec(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b,
+                                       x.scale, out, ns), 20, 3)
+    o2, n2 = torch.empty_like(out), torch.empty_like(ns)
+    t_ours = _device_us(lambda: K.gdn_decode(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias,
+                                             x.b, x.scale, o2, n2), 20, 3)
+    print(f"decode qk4_v8 B=64: reference kernel {t_ref:.1f} us, this package {t_ours:.1f} us")
+    torch.testing.assert_close(o2.float(), out.float(), **DECODE_OUT_TOL)
+    assert t_ours * 1.5 < t_ref
+
+    lengths = [8192]
+    x = W.make_prefill_inputs(lengths, seed=2, h_qk=4, h_v=8, device="cuda",
+                              cu_dtype=torch.int64)
+    out = torch.empty(8192, 8, 128, dtype=torch.bfloat16, device="cuda")
+    ns = torch.empty(1, 8, 128, 128, dtype=torch.float32, device="cuda")
+    t_ref = _device_us(lambda: ref_pre(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b,
+                                       x.cu_seqlens, x.scale, out, ns), 2)
+    o2, n2 = torch.empty_like(out), torch.empty_like(ns)
+    t_ours = _device_us(lambda: K.gdn_prefill(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias,
+                                              x.b, x.cu_seqlens, x.scale, o2, n2), 10, 2)
+    print(f"prefill qk4_v8 T=8192: reference kernel {t_ref:.1f} us, this package {t_ours:.1f} us")
+    assert_prefill_close(o2.cpu(), n2.cpu(), out.cpu(), ns.cpu(), lengths)
+    assert t_ours * 20 < t_ref
