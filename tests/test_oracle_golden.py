@@ -121,6 +121,24 @@ def test_chunked_matches_sequential_ragged():
     torch.testing.assert_close(s1, s2, atol=1e-5, rtol=1e-4)
 
 
+def test_chunk_states_are_the_token_recurrence_at_chunk_ends():
+    """The per-chunk states the chunked oracle reports (the state entering each
+    chunk, ref prefill_design.md:600-606 asks tests to compare these) equal the
+    token-by-token recurrence stopped at each chunk end."""
+    x = W.make_prefill_inputs([200], seed=12, h_qk=2, h_v=4)
+    _, fin, cs = O.prefill_chunked(x.q, x.k, x.v, x.state, x.A_log, x.a, x.dt_bias, x.b,
+                                   x.cu_seqlens, x.scale, return_chunk_states=True)
+    assert cs[0].shape[0] == 4   # chunks of 64, 64, 64, 8 tokens
+    for j, end in enumerate((0, 64, 128, 192)):
+        if end == 0:
+            torch.testing.assert_close(cs[0][0], x.state[0])
+            continue
+        cu = torch.tensor([0, end], dtype=x.cu_seqlens.dtype)
+        _, s_seq = O.prefill_sequential(x.q[:end], x.k[:end], x.v[:end], x.state, x.A_log,
+                                        x.a[:end], x.dt_bias, x.b[:end], cu, x.scale)
+        torch.testing.assert_close(cs[0][j], s_seq[0], atol=1e-5, rtol=1e-4)
+
+
 def _mtp_fixture_inputs(g):
     x = W.make_pool_decode_inputs(3, 3, 5, seed=21, h_qk=1, h_v=2)
     for n in ("q", "k", "v", "pool", "A_log", "a", "dt_bias", "b"):

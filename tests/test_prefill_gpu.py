@@ -8,7 +8,8 @@ import pytest
 import torch
 
 from conftest import GOLDEN
-from helpers import PREFILL_OUT_TOL, assert_prefill_close, rel_fro, to_dev
+from helpers import (PREFILL_OUT_TOL, PREFILL_STATE_REL_FRO, assert_prefill_close, rel_fro,
+                     to_dev)
 from gdn_kernel_b200 import _lib, kernel as K, workloads as W
 from oracle import gdn_oracle as O
 
@@ -118,6 +119,35 @@ def test_prefill_config2_T8192_drift(path):
     d = (out.float() - ro.float()).abs()
     print(f"\n[T=8192 drift, {path}] output max-abs {d.max().item():.3e} mean-abs {d.mean().item():.3e}; "
           f"final state rel-Frobenius max {err.max().item():.3e}")
+
+
+def test_prefill_intermediate_chunk_states(path):
+    """The state at every chunk boundary, as the reference's prefill design asks
+    tests to compare (ref prefill_design.md:600-606).  One call whose sequences
+    are prefixes of the same 500-token stream (1 to 7 whole chunks, a ragged
+    100 tokens, and the whole stream), each from the same initial state, returns
+    the state after every chunk; each is compared with the state the oracle
+    carries into the next chunk of the whole stream.  The packed call's outputs
+    and states are checked against the oracle too."""
+    import types
+    base = W.make_prefill_inputs([500], seed=81)
+    ends = [64 * j for j in range(1, 8)] + [100, 500]
+    cat = lambda t: torch.cat([t[:e] for e in ends])
+    cu = torch.tensor([0] + [sum(ends[:i + 1]) for i in range(len(ends))], dtype=torch.int32)
+    x = types.SimpleNamespace(q=cat(base.q), k=cat(base.k), v=cat(base.v),
+                              state=base.state.expand(len(ends), -1, -1, -1).contiguous(),
+                              A_log=base.A_log, a=cat(base.a), dt_bias=base.dt_bias,
+                              b=cat(base.b), cu_seqlens=cu, scale=base.scale)
+    out, ns = _run(x, path)
+    ro, rs = _oracle(x)
+    assert_prefill_close(out, ns, ro, rs, ends)
+    _, fin, cs = O.prefill_chunked(base.q, base.k, base.v, base.state, base.A_log, base.a,
+                                   base.dt_bias, base.b, base.cu_seqlens, base.scale,
+                                   return_chunk_states=True)
+    for j in range(1, 8):   # the prefix of j chunks ends where chunk j of the stream starts
+        err = rel_fro(ns[j - 1:j], cs[0][j:j + 1])
+        assert err.max().item() <= PREFILL_STATE_REL_FRO, (j, err.max().item())
+    assert rel_fro(ns[-1:], fin).max().item() <= PREFILL_STATE_REL_FRO
 
 
 def test_prefill_config3_varlen16(path):
